@@ -1,0 +1,433 @@
+"""Benchmark of the voxtral.cpp attention node on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vtx|reference]
+                    [--workload encoder|decode]
+
+Headline workload: the Whisper-large-shaped audio
+encoder self-attention of voxtral.cpp (src/voxtral.cpp:1611): one 30 s clip ->
+1500 frames, 20 heads x head_dim 64, 32 layers, bidirectional (mask = NULL),
+f16 Q/K/V drawn N(0,1) from a seed, fp32 softmax/accumulate.  One step = the
+32 attention calls of one clip, each layer with its own Q/K/V (368 MB per step,
+larger than the 126 MB L2, so no flush is needed between steps).  Metric:
+attention TFLOP/s = 4 * D * H * n_q * n_kv * layers / time.
+
+--workload decode times configs[4] instead: 256 ragged streams (n_kv ~ U[512,
+16384]), GQA 32/8 x 128, f16 KV, one decode token per stream; one step = one
+layer's attention for all streams (KV GB/s).
+
+Multi-GPU: one process per GPU (torchrun); each rank attends its own clips /
+streams (weak scaling, no collective on the data path); time = max over ranks.
+--impl reference times the CPU restatement of ggml's flash_attn_ext (the
+oracle; ggml itself is not buildable here) on a bounded sample of the same
+workload with every host core, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "voxtral.cpp_b200"))
+
+ENC = dict(n=1500, H=20, D=64, layers=32)
+DEC = dict(n_seq=256, Hq=32, Hkv=8, D=128, lo=512, hi=16384)
+METRIC_ENC = "attn TFLOP/s (prefill/encoder)"
+METRIC_DEC = "KV GB/s (decode)"
+
+
+def load_peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            j = json.load(f)
+        return {"hbm_gbs": j["hbm_gbs"], "bf16_tflops": j["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True,
+                                     timeout=5).stdout.strip()
+                if out:
+                    self.samples.append([x.strip() for x in out.split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def __enter__(self):
+        self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = sorted(float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit())
+        mx = max((float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()), default=None)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for i, n in enumerate(names):
+                if len(s) > 5 + i and s[5 + i].lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(self.samples)}
+
+
+# ------------------------------------------------------------------------------
+def dist_setup(n_gpus: int):
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier_max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda", dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+# ---- encoder workload ------------------------------------------------------------
+def enc_flops_per_layer():
+    return 4.0 * ENC["D"] * ENC["H"] * ENC["n"] * ENC["n"]
+
+
+def make_encoder_inputs(seed: int, device):
+    """Per layer: contiguous [D, H, n] f16 buffers (ggml order) permuted to the
+    [D, n, H] views voxtral.cpp passes (src/voxtral.cpp:1601-1605)."""
+    import torch
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    n, H, D, L = ENC["n"], ENC["H"], ENC["D"], ENC["layers"]
+    qkv = torch.randn((L, 3, n, H, D), generator=g, device=device, dtype=torch.float32).to(torch.float16)
+    return qkv
+
+
+def enc_views(buf_l):
+    # buf_l: (3, n, H, D) -> q, k, v views (1, H, n, D)
+    return [buf_l[i].permute(1, 0, 2).unsqueeze(0) for i in range(3)]
+
+
+def run_encoder(args, rank, world, local):
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    L, n, H, D = ENC["layers"], ENC["n"], ENC["H"], ENC["D"]
+    qkv = make_encoder_inputs(1234 + rank, dev)
+    out = torch.empty((L, 1, n, H, D), device=dev, dtype=torch.float32)
+    scale = 1.0 / D ** 0.5
+    views = [enc_views(qkv[l]) for l in range(L)]
+    stream = torch.cuda.Stream(device=dev)
+    ws = torch.empty(max(1, vtx_attn.workspace_bytes(*views[0], scale)), dtype=torch.uint8, device=dev)
+
+    def step():
+        for l in range(L):
+            q, k, v = views[l]
+            vtx_attn.flash_attn_ext(q, k, v, None, scale, out=out[l], workspace=ws, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        step()
+    torch.cuda.synchronize()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize()
+
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for _ in range(args.steps):
+                graph.replay()
+            e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = e0.elapsed_time(e1)
+    ms = barrier_max(ms_local, world)
+    flop_step = enc_flops_per_layer() * L
+    value = flop_step * args.steps * world / (ms * 1e-3) / 1e12
+    launch_ms = ms_local / (args.steps * L)
+    err = vtx_attn.read_device_error(stream)
+
+    # ---- end to end through the public call, host buffers ----------------------
+    e2e = run_encoder_e2e(args, dev, world, rank)
+
+    peaks = load_peaks()
+    achieved = enc_flops_per_layer() / (launch_ms * 1e-3) / 1e12
+    res = {
+        "metric": METRIC_ENC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic N(0,1) f16 Q/K/V, seeded per rank (no dataset; BASELINE configs[1] shapes)",
+        "config": {"workload": "configs[1] audio-encoder self-attention, 30 s clip: 1500 frames, 20 heads x 64, "
+                               "32 layers, bidirectional, batch 1 per GPU",
+                   "per_step": "32 layer calls (one clip), CUDA-graph replay",
+                   "l2": "inputs larger than L2 (368 MB of Q/K/V per step), no flush",
+                   "parallelism": f"dp{world} (independent clips per GPU)",
+                   "audio_sec_per_step_per_gpu": 30},
+        "audio_sec_per_sec": round(30.0 * args.steps * world / (ms * 1e-3), 1),
+        "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
+                     "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
+                     "traffic": None, "peak_src": f"{peaks['src']} bf16 dense (burst)",
+                     "per_launch_ms": round(launch_ms, 5),
+                     "per_launch_flop": enc_flops_per_layer()},
+        "e2e": e2e,
+        "gpu_launches": args.steps * L,
+        "clocks": clocks.summary(),
+        "device_error": err,
+    }
+    return res
+
+
+def run_encoder_e2e(args, dev, world, rank):
+    """Host Q/K/V (pinned) -> device -> vtx_flash_attn_ext -> host output, per
+    layer, copies on their own streams overlapped with the attention calls."""
+    import torch
+    import vtx_attn
+
+    L, n, H, D = ENC["layers"], ENC["n"], ENC["H"], ENC["D"]
+    scale = 1.0 / D ** 0.5
+    host_in = make_encoder_inputs(99 + rank, dev).cpu().pin_memory()          # (L, 3, n, H, D)
+    host_out = torch.empty((L, 1, n, H, D), dtype=torch.float32).pin_memory()
+    nbuf = 3
+    dbuf = [torch.empty((3, n, H, D), device=dev, dtype=torch.float16) for _ in range(nbuf)]
+    dout = [torch.empty((1, n, H, D), device=dev, dtype=torch.float32) for _ in range(nbuf)]
+    s_h2d, s_cmp, s_d2h = (torch.cuda.Stream(device=dev) for _ in range(3))
+    ws = torch.empty(max(1, vtx_attn.workspace_bytes(*enc_views(dbuf[0]), scale)), dtype=torch.uint8, device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(nbuf)]
+    ev_cmp = [torch.cuda.Event() for _ in range(nbuf)]
+    ev_out = [torch.cuda.Event() for _ in range(nbuf)]
+
+    def one_clip():
+        for l in range(L):
+            b = l % nbuf
+            if l >= nbuf:
+                s_h2d.wait_event(ev_cmp[b])
+            with torch.cuda.stream(s_h2d):
+                dbuf[b].copy_(host_in[l], non_blocking=True)
+                ev_in[b].record(s_h2d)
+            s_cmp.wait_event(ev_in[b])
+            if l >= nbuf:
+                s_cmp.wait_event(ev_out[b])
+            q, k, v = enc_views(dbuf[b])
+            vtx_attn.flash_attn_ext(q, k, v, None, scale, out=dout[b], workspace=ws, stream=s_cmp)
+            ev_cmp[b].record(s_cmp)
+            s_d2h.wait_event(ev_cmp[b])
+            with torch.cuda.stream(s_d2h):
+                host_out[l].copy_(dout[b], non_blocking=True)
+                ev_out[b].record(s_d2h)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        one_clip()
+    torch.cuda.synchronize()
+    steps = max(1, min(args.steps, 10))
+    barrier(world)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        one_clip()
+    torch.cuda.synchronize()
+    dt = barrier_max(time.perf_counter() - t0, world)
+    h2d = host_in[0].numel() * host_in.element_size() * L
+    d2h = host_out[0].numel() * host_out.element_size() * L
+    return {"value": round(enc_flops_per_layer() * L * steps * world / dt / 1e12, 3), "unit": "TFLOP/s",
+            "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "how": "pinned host Q/K/V per layer -> H2D stream, vtx_flash_attn_ext on compute stream, "
+                   "D2H stream; host wall clock after synchronize, max over ranks"}
+
+
+# ---- CPU baseline (oracle = CPU restatement of ggml's flash_attn_ext) -----------
+def cpu_baseline_encoder(budget_s: float = 15.0):
+    import numpy as np
+    import oracle as O
+    n, H, D = ENC["n"], ENC["H"], ENC["D"]
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((n, H, D)).astype(np.float16)
+    k = rng.standard_normal((n, H, D)).astype(np.float16)
+    v = rng.standard_normal((n, H, D)).astype(np.float16)
+    view = lambda a: a.transpose(1, 0, 2)[None]
+    cores = O.n_cores()
+    rows = 64
+    t0 = time.perf_counter()
+    O.flash_attn_ext(view(q[:rows]), view(k), view(v), None, 0.125, threads=cores)
+    dt = time.perf_counter() - t0
+    rows = int(min(n, max(rows, rows * budget_s / max(dt, 1e-3) * 0.5)))
+    t0 = time.perf_counter()
+    O.flash_attn_ext(view(q[:rows]), view(k), view(v), None, 0.125, threads=cores)
+    dt = time.perf_counter() - t0
+    flops = 4.0 * D * H * rows * n
+    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"1 layer: {rows} query rows x {n} keys x {H} heads x {D} (of 1500 x 32 layers), "
+                      f"ggml-mode oracle, {dt:.2f} s"}
+
+
+# ---- decode workload ---------------------------------------------------------------
+def run_decode(args, rank, world, local):
+    import numpy as np
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    S, Hq, Hkv, D = DEC["n_seq"], DEC["Hq"], DEC["Hkv"], DEC["D"]
+    rng = np.random.default_rng(4321 + rank)
+    lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(77 + rank)
+    ks, vs = [], []
+    for L in lens:
+        ks.append(torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16))
+        vs.append(torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16))
+    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D, vtx_attn.F16,
+                                    Hkv * D * 2, D * 2, int(lens.max()), 1.0 / D ** 0.5)
+    q = torch.randn((S, Hq, D), generator=g, device=dev)
+    out = torch.empty_like(q)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(max(1, args.warmup)):
+            plan(q, out, stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            plan(q, out, stream)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = e0.elapsed_time(e1)
+    ms = barrier_max(ms_local, world)
+    kv_bytes = float(lens.astype(np.int64).sum()) * Hkv * D * 2 * 2
+    value = kv_bytes * args.steps * world / (ms * 1e-3) / 1e9
+    peaks = load_peaks()
+    achieved = kv_bytes / (ms_local / args.steps * 1e-3) / 1e9
+    return {
+        "metric": METRIC_DEC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic N(0,1) f16 KV, ragged lengths U[512,16384] seeded per rank",
+        "config": {"workload": "configs[4] batched decode: 256 streams, GQA 32/8 x 128, f16 KV, 1 layer per step",
+                   "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.1f} GB KV per step)",
+                   "parallelism": f"dp{world} (independent streams per GPU)"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "peak_src": f"{peaks['src']} copy bandwidth"},
+        "gpu_launches": args.steps * 2,
+        "clocks": clocks.summary(),
+    }
+
+
+# ---- reference arm ------------------------------------------------------------------
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return None
+    import oracle as O
+    O.build()
+    vals = []
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_baseline_encoder(budget_s=2.0)
+    for _ in range(max(1, min(args.steps, 3))):
+        vals.append(cpu_baseline_encoder(budget_s=10.0))
+    v = sorted(x["value"] for x in vals)[len(vals) // 2]
+    cb = dict(vals[0])
+    cb["value"] = v
+    return {"impl": "reference", "metric": METRIC_ENC, "value": v, "unit": "TFLOP/s",
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(vals), "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) f16 Q/K/V (BASELINE configs[1] shapes)",
+            "config": {"workload": "configs[1] audio-encoder self-attention, 30 s clip: 1500 frames, 20 heads x 64, "
+                                   "32 layers, bidirectional, batch 1 per GPU",
+                       "reference": "CPU restatement of ggml-cpu flash_attn_ext (oracle/vtx_ref.c); ggml@5cecdad "
+                                    "is fetched at configure time by the reference and is not present here"},
+            "cpu_baseline": cb,
+            "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+
+    if args.impl == "reference":
+        res = run_reference(args)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    import torch
+    import vtx_attn
+    vtx_attn.load()
+    rank, world, local = dist_setup(args.gpus)
+    if args.workload == "encoder":
+        res = run_encoder(args, rank, world, local)
+        if rank == 0 and world == 1 and not args.no_cpu_baseline:
+            res["cpu_baseline"] = cpu_baseline_encoder()
+    else:
+        res = run_decode(args, rank, world, local)
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,172 @@
+/*
+ * vtx_fa.h — C ABI of the B200 (sm_100a) attention node for voxtral.cpp.
+ *
+ * This library replaces exactly one ggml graph node: GGML_OP_FLASH_ATTN_EXT,
+ * created by
+ *     ggml_flash_attn_ext(ctx, q, k, v, mask, scale, max_bias, logit_softcap)
+ * at the two call sites of voxtral.cpp:
+ *     src/voxtral.cpp:1611  encoder self-attention (offline: mask = NULL;
+ *                           realtime: F16 sliding-causal mask, window 750)
+ *     src/voxtral.cpp:1802  decoder GQA attention over the KV cache
+ *                           (prefill: F16 causal mask; decode step: NULL)
+ * The arithmetic it replaces lives in ggml (fetched by CMake FetchContent at
+ * ggml-org/ggml@5cecdad, reference CMakeLists.txt:33-41): the CPU kernel
+ * ggml_compute_forward_flash_attn_ext_f16 and the ggml-cuda fattn-* kernels.
+ *
+ * Tensor descriptors mirror ggml_tensor's geometry: ne[0] is the fastest
+ * dimension, nb[i] are byte strides, any permuted view is accepted as is
+ * (the call sites pass ggml_permute views, src/voxtral.cpp:1601-1605 and
+ * :1783-1794).  Type ids are ggml's (GGML_TYPE_F32 = 0, F16 = 1, Q8_0 = 8).
+ *
+ * Operator contract (ggml semantics):
+ *   q    [Dk, n_q,  Hq,  B]   F32 or F16
+ *   k    [Dk, n_kv, Hkv, B]   F32, F16 or Q8_0 (Hq % Hkv == 0 -> GQA broadcast)
+ *   v    [Dv, n_kv, Hkv, B]   same type as k, rows are tokens (not transposed)
+ *   mask [n_kv, >= n_q, 1|Hq, 1|B]  F16, additive, -inf = skip; may be NULL
+ *   dst  [Dv, Hq, n_q, B]     F32, written by the call (ggml permutes the
+ *                             result so one token's heads are contiguous)
+ *   O[b,i,h,:] = sum_j softmax_j(scale*q.k_j [softcap] + slope_h*mask[i,j]) v_j
+ *
+ * All device pointers belong to the caller.  No entry point allocates device
+ * memory, synchronises the host or aborts: errors are returned as negative
+ * codes (vtx_strerror).  Scratch memory for split-KV partials and dtype
+ * conversion is passed in as `workspace`; its size comes from the matching
+ * *_workspace() query.  `stream` is a cudaStream_t (NULL = legacy stream).
+ */
+#ifndef VTX_FA_H
+#define VTX_FA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define VTX_API __attribute__((visibility("default")))
+#else
+#define VTX_API
+#endif
+
+#define VTX_FA_ABI_VERSION 1
+
+/* ggml type ids (ggml/include/ggml.h enum ggml_type) */
+enum vtx_type {
+    VTX_TYPE_F32  = 0,
+    VTX_TYPE_F16  = 1,
+    VTX_TYPE_Q8_0 = 8
+};
+
+/* Q8_0 block, identical to ggml's block_q8_0: 32 values = d * qs[i]. */
+#define VTX_QK8_0 32
+typedef struct {
+    uint16_t d;              /* IEEE half scale */
+    int8_t   qs[VTX_QK8_0];
+} vtx_block_q8_0;            /* 34 bytes, 2-byte aligned */
+
+/* Status codes. */
+enum vtx_status {
+    VTX_OK                  =  0,
+    VTX_ERR_NULL            = -1,  /* a required pointer is NULL            */
+    VTX_ERR_TYPE            = -2,  /* unsupported or mismatched dtype       */
+    VTX_ERR_SHAPE           = -3,  /* inconsistent shapes                   */
+    VTX_ERR_STRIDE          = -4,  /* stride/alignment not supported        */
+    VTX_ERR_UNSUPPORTED     = -5,  /* head_dim / parameter not supported    */
+    VTX_ERR_WORKSPACE       = -6,  /* workspace too small or misaligned     */
+    VTX_ERR_CUDA            = -7,  /* a CUDA launch/runtime call failed     */
+    VTX_ERR_NO_DEVICE       = -8   /* no sm_100 device is current           */
+};
+
+/* Mirrors the geometry of a ggml_tensor (ggml.h struct ggml_tensor:
+ * type, ne[GGML_MAX_DIMS], nb[GGML_MAX_DIMS], data). */
+typedef struct vtx_tensor {
+    int32_t type;            /* enum vtx_type */
+    int32_t reserved;
+    int64_t ne[4];           /* elements per dim, ne[0] fastest */
+    size_t  nb[4];           /* byte strides; nb[0] = type size (34 for a Q8_0 block) */
+    void   *data;            /* device pointer */
+} vtx_tensor;
+
+/* Operator parameters.  scale/max_bias/logit_softcap are ggml_flash_attn_ext's
+ * op_params (ggml.h).  causal/window are an exact, tensor-free encoding of the
+ * masks voxtral.cpp builds on the host:
+ *   causal = 1 : query i may see key j iff j <= i + (n_kv - n_q)
+ *                (src/voxtral.cpp:2103-2111 fill_causal_mask, n_kv == n_q)
+ *   window = W : additionally j >= i + (n_kv - n_q) - (W - 1)
+ *                (src/voxtral.cpp:2181-2188, VOXTRAL_ENC_WINDOW = 750)
+ * An explicit mask tensor, if given, is applied on top. */
+typedef struct vtx_fa_params {
+    float   scale;
+    float   max_bias;        /* ALiBi; 0 = off (both voxtral call sites) */
+    float   logit_softcap;   /* 0 = off (both voxtral call sites) */
+    int32_t causal;          /* 0 / 1 */
+    int32_t window;          /* 0 = no window, else W > 0 (requires causal) */
+    int32_t reserved[3];
+} vtx_fa_params;
+
+/* ggml_flash_attn_ext replacement (reference: ggml.h ggml_flash_attn_ext,
+ * called at src/voxtral.cpp:1611 and src/voxtral.cpp:1802).
+ * Returns VTX_OK or a negative vtx_status.  Asynchronous on `stream`. */
+VTX_API int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v,
+                       const vtx_tensor *mask, const vtx_fa_params *params,
+                       vtx_tensor *dst, void *workspace, size_t workspace_bytes,
+                       void *stream);
+
+/* Bytes of workspace vtx_flash_attn_ext needs for these operands (0 is a valid
+ * answer).  Pure host computation; never touches the device.  Returns
+ * (size_t)-1 if the operands are rejected. */
+VTX_API size_t vtx_flash_attn_ext_workspace(const vtx_tensor *q, const vtx_tensor *k,
+                                    const vtx_tensor *v, const vtx_fa_params *params);
+
+/* Batched ragged decode: one new token per stream, each stream with its own
+ * KV cache and length.  This is the decode node of src/voxtral.cpp:1802
+ * (n_tokens = 1, mask = NULL, reached from run_decoder_step :2438 and
+ * run_offline_step :2506) executed for many independent streams in one call.
+ *   q        : device F32 [n_seq][n_head_q][head_dim], contiguous
+ *   k_ptrs   : device array of n_seq device pointers, one per stream; the
+ *              stream's keys are rows at k_ptrs[s] + t*kv_nb1 + g*kv_nb2
+ *   v_ptrs   : same for values
+ *   kv_len   : device int32 [n_seq], keys 0..kv_len[s]-1 are attended
+ *   dst      : device F32 [n_seq][n_head_q][head_dim]
+ * max_kv_len bounds every kv_len[s] (host-known upper bound used for sizing). */
+typedef struct vtx_decode_batch {
+    int32_t n_seq;
+    int32_t n_head_q;
+    int32_t n_head_kv;
+    int32_t head_dim;
+    int32_t kv_type;         /* VTX_TYPE_F16, VTX_TYPE_Q8_0 or VTX_TYPE_F32 */
+    int32_t max_kv_len;
+    size_t  kv_nb1;          /* byte stride between tokens */
+    size_t  kv_nb2;          /* byte stride between kv heads */
+    const float        *q;
+    const void * const *k_ptrs;
+    const void * const *v_ptrs;
+    const int32_t      *kv_len;
+    float              *dst;
+    float   scale;
+    int32_t reserved;
+} vtx_decode_batch;
+
+VTX_API int vtx_flash_attn_decode_batched(const vtx_decode_batch *batch, void *workspace,
+                                  size_t workspace_bytes, void *stream);
+
+VTX_API size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *batch);
+
+/* Diagnostic: synchronises `stream`, returns and clears the device-side error
+ * word of the current device (0 = none).  Kernels set it instead of hanging
+ * when a bounded pipeline wait runs out, or when a batched-decode stream base
+ * is not aligned to the copy width.  No counterpart in ggml (ggml aborts). */
+VTX_API int vtx_read_device_error(void *stream);
+
+/* Human-readable text for a vtx_status. */
+VTX_API const char *vtx_strerror(int status);
+
+/* VTX_FA_ABI_VERSION of the loaded library. */
+VTX_API int vtx_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VTX_FA_H */

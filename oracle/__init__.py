@@ -1,0 +1,222 @@
+"""CPU oracle for the voxtral.cpp attention node — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, ``__graft_entry__.smoke()`` and ``bench.py``'s CPU-baseline leg
+use this package, as the checker.  The product package (voxtral.cpp_b200)
+never imports it.
+
+``vtx_ref.c`` restates ggml's CPU ``flash_attn_ext`` numerics
+(ggml/src/ggml-cpu/ops.cpp ``ggml_compute_forward_flash_attn_ext_f16`` at
+ggml@5cecdad, the revision pinned by reference CMakeLists.txt:33-41) and an
+fp64 "truth" mode.  Parity at the op level is UNPINNED against ggml itself
+(no ggml source/binary here; the reference's tests only pin end-to-end logits
+that need absent weights).  Pinned pieces: Q8_0 bytes vs gguf-py 0.19.0,
+fp64 mode vs torch float64 attention (tests/golden/).
+
+Tensors are numpy arrays in ggml geometry read back to front: an array of
+shape (B, H, n, D) with arbitrary strides is the ggml view [D, n, H, B] with
+nb = strides reversed.  Q8_0 tensors are uint8 arrays whose last axis holds
+D/32 blocks of 34 bytes.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libvtx_ref.so")
+_lib = None
+
+F32, F16, Q8_0 = 0, 1, 8
+QK8_0 = 32
+Q8_0_BLOCK = 34
+MODE_GGML, MODE_FP64 = 0, 1
+
+
+class Tensor(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4),
+                ("data", ctypes.c_void_p)]
+
+
+class Params(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_float), ("max_bias", ctypes.c_float),
+                ("logit_softcap", ctypes.c_float), ("causal", ctypes.c_int32),
+                ("window", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
+class DecodeBatch(ctypes.Structure):
+    _fields_ = [("n_seq", ctypes.c_int32), ("n_head_q", ctypes.c_int32),
+                ("n_head_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("kv_type", ctypes.c_int32), ("max_kv_len", ctypes.c_int32),
+                ("kv_nb1", ctypes.c_size_t), ("kv_nb2", ctypes.c_size_t),
+                ("q", ctypes.c_void_p), ("k_ptrs", ctypes.c_void_p),
+                ("v_ptrs", ctypes.c_void_p), ("kv_len", ctypes.c_void_p),
+                ("dst", ctypes.c_void_p), ("scale", ctypes.c_float),
+                ("reserved", ctypes.c_int32)]
+
+
+def build(force: bool = False) -> str:
+    """Compile vtx_ref.c (make) unless the library is already there."""
+    src = os.path.join(_HERE, "vtx_ref.c")
+    if force or not os.path.exists(_LIB_PATH) or os.path.getmtime(_LIB_PATH) < os.path.getmtime(src):
+        subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(_LIB_PATH)
+        vp, i64 = ctypes.c_void_p, ctypes.c_int64
+        for name in ("vtx_ref_quantize_q8_0", "vtx_ref_quantize_q8_0_rne",
+                     "vtx_ref_dequantize_q8_0", "vtx_ref_f32_to_f16", "vtx_ref_f16_to_f32"):
+            getattr(L, name).argtypes = [vp, vp, i64]
+            getattr(L, name).restype = None
+        L.vtx_ref_flash_attn_ext.argtypes = [ctypes.POINTER(Tensor)] * 4 + [
+            ctypes.POINTER(Params), ctypes.POINTER(Tensor), ctypes.c_int, ctypes.c_int]
+        L.vtx_ref_flash_attn_ext.restype = ctypes.c_int
+        L.vtx_ref_decode_batched.argtypes = [ctypes.POINTER(DecodeBatch), ctypes.c_int, ctypes.c_int]
+        L.vtx_ref_decode_batched.restype = ctypes.c_int
+        _lib = L
+    return _lib
+
+
+def n_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+# ---- formats ------------------------------------------------------------
+
+def quantize_q8_0(x: np.ndarray) -> np.ndarray:
+    """ggml quantize_row_q8_0_ref over the last axis (multiple of 32).
+    Returns uint8 with last axis D/32*34."""
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    D = x.shape[-1]
+    assert D % QK8_0 == 0
+    out = np.empty(x.shape[:-1] + (D // QK8_0 * Q8_0_BLOCK,), dtype=np.uint8)
+    lib().vtx_ref_quantize_q8_0(x.ctypes.data, out.ctypes.data, x.size)
+    return out
+
+
+def dequantize_q8_0(b: np.ndarray) -> np.ndarray:
+    b = np.ascontiguousarray(b, dtype=np.uint8)
+    D = b.shape[-1] // Q8_0_BLOCK * QK8_0
+    out = np.empty(b.shape[:-1] + (D,), dtype=np.float32)
+    lib().vtx_ref_dequantize_q8_0(b.ctypes.data, out.ctypes.data, out.size)
+    return out
+
+
+def to_f16(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.float16)
+    lib().vtx_ref_f32_to_f16(x.ctypes.data, out.ctypes.data, x.size)
+    return out
+
+
+# ---- tensors --------------------------------------------------------------
+
+def tensor(a: np.ndarray, ttype: int | None = None) -> Tensor:
+    """ggml descriptor for a numpy array (shape reversed = ne)."""
+    if a.ndim > 4:
+        raise ValueError("at most 4 dims")
+    shape = (1,) * (4 - a.ndim) + tuple(a.shape)
+    strides = (0,) * (4 - a.ndim) + tuple(a.strides)
+    if ttype is None:
+        ttype = {np.dtype(np.float32): F32, np.dtype(np.float16): F16}[a.dtype]
+    t = Tensor()
+    t.type = ttype
+    ne = list(reversed(shape))
+    nb = list(reversed(strides))
+    if ttype == Q8_0:
+        ne[0] = ne[0] // Q8_0_BLOCK * QK8_0
+        nb[0] = Q8_0_BLOCK
+    # broadcast dims of size 1 get a consistent stride
+    for i in range(1, 4):
+        if nb[i] == 0:
+            nb[i] = nb[i - 1] * (ne[i - 1] if i > 1 or ttype != Q8_0 else ne[0] // QK8_0)
+    for i in range(4):
+        t.ne[i] = ne[i]
+        t.nb[i] = nb[i]
+    t.data = a.ctypes.data
+    return t
+
+
+def params(scale: float, max_bias: float = 0.0, softcap: float = 0.0,
+           causal: int = 0, window: int = 0) -> Params:
+    p = Params()
+    p.scale, p.max_bias, p.logit_softcap = scale, max_bias, softcap
+    p.causal, p.window = int(causal), int(window)
+    return p
+
+
+def flash_attn_ext(q: np.ndarray, k: np.ndarray, v: np.ndarray, mask: np.ndarray | None,
+                   scale: float, max_bias: float = 0.0, softcap: float = 0.0,
+                   causal: int = 0, window: int = 0, kv_type: int | None = None,
+                   mode: int = MODE_GGML, threads: int | None = None) -> np.ndarray:
+    """Run the oracle.  q: (B, Hq, n_q, D) view; k/v: (B, Hkv, n_kv, D[bytes]);
+    mask: (n_q', n_kv) F16 or (B|1, Hq|1, n_q', n_kv) or None.
+    Returns dst as float32 (B, n_q, Hq, Dv) — ggml's [Dv, Hq, n_q, B]."""
+    tq = tensor(q)
+    tk = tensor(k, kv_type)
+    tv = tensor(v, kv_type)
+    B, Hq, n_q = tq.ne[3], tq.ne[2], tq.ne[1]
+    Dv = tv.ne[0]
+    dst = np.zeros((B, n_q, Hq, Dv), dtype=np.float32)
+    td = tensor(dst)
+    tm = tensor(mask, F16) if mask is not None else None
+    p = params(scale, max_bias, softcap, causal, window)
+    rc = lib().vtx_ref_flash_attn_ext(ctypes.byref(tq), ctypes.byref(tk), ctypes.byref(tv),
+                                      ctypes.byref(tm) if tm is not None else None,
+                                      ctypes.byref(p), ctypes.byref(td), mode,
+                                      threads or n_cores())
+    if rc != 0:
+        raise ValueError(f"oracle rejected operands: status {rc}")
+    return dst
+
+
+def decode_batched(q: np.ndarray, k_list, v_list, kv_len, scale: float, kv_type: int,
+                   n_head_kv: int, kv_nb1: int, kv_nb2: int, mode: int = MODE_GGML,
+                   threads: int | None = None) -> np.ndarray:
+    """Host version of vtx_flash_attn_decode_batched.  q: (n_seq, Hq, D) f32;
+    k_list/v_list: per-stream numpy buffers (any dtype, byte-addressed with
+    kv_nb1 per token and kv_nb2 per head)."""
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    n_seq, Hq, D = q.shape
+    dst = np.zeros_like(q)
+    kp = (ctypes.c_void_p * n_seq)(*[a.ctypes.data for a in k_list])
+    vp = (ctypes.c_void_p * n_seq)(*[a.ctypes.data for a in v_list])
+    kl = np.ascontiguousarray(kv_len, dtype=np.int32)
+    b = DecodeBatch()
+    b.n_seq, b.n_head_q, b.n_head_kv, b.head_dim = n_seq, Hq, n_head_kv, D
+    b.kv_type, b.max_kv_len = kv_type, int(kl.max()) if n_seq else 0
+    b.kv_nb1, b.kv_nb2 = kv_nb1, kv_nb2
+    b.q, b.k_ptrs, b.v_ptrs = q.ctypes.data, ctypes.addressof(kp), ctypes.addressof(vp)
+    b.kv_len, b.dst, b.scale = kl.ctypes.data, dst.ctypes.data, scale
+    rc = lib().vtx_ref_decode_batched(ctypes.byref(b), mode, threads or n_cores())
+    if rc != 0:
+        raise ValueError(f"oracle rejected batch: status {rc}")
+    return dst
+
+
+# ---- reference masks (host-built, exactly as voxtral.cpp fills them) ------
+
+def causal_mask(n: int) -> np.ndarray:
+    """src/voxtral.cpp:2103-2111 fill_causal_mask, cast to F16 (:1801)."""
+    m = np.zeros((n, n), dtype=np.float32)
+    m[np.triu_indices(n, 1)] = -np.inf
+    return m.astype(np.float16)
+
+
+def window_mask(n: int, window: int = 750) -> np.ndarray:
+    """src/voxtral.cpp:2181-2188 sliding causal mask (chunk-local), F16 (:1564)."""
+    qi = np.arange(n)[:, None]
+    kj = np.arange(n)[None, :]
+    allow = (kj <= qi) & (kj >= np.maximum(0, qi - (window - 1)))
+    return np.where(allow, 0.0, -np.inf).astype(np.float16)

@@ -1,0 +1,106 @@
+"""CPU tests of the C-ABI boundary: the library builds and loads, exports every
+symbol include/vtx_fa.h declares, its struct layouts match the ctypes mirrors,
+and operand validation answers with status codes before touching a device."""
+import ctypes
+import os
+import re
+import subprocess
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "vtx_fa.h")
+
+
+def declared_symbols():
+    text = open(HEADER).read()
+    return re.findall(r"VTX_API\s+[\w\s\*]+?\b(vtx_\w+)\s*\(", text)
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import build as b  # voxtral.cpp_b200/build.py
+    b.build()
+    import vtx_attn
+    return vtx_attn.load()
+
+
+def test_header_declares_the_entry_points():
+    syms = set(declared_symbols())
+    assert {"vtx_flash_attn_ext", "vtx_flash_attn_ext_workspace", "vtx_flash_attn_decode_batched",
+            "vtx_flash_attn_decode_batched_workspace", "vtx_strerror", "vtx_abi_version",
+            "vtx_read_device_error"} <= syms
+
+
+def test_library_exports_every_declared_symbol(lib):
+    out = subprocess.run(["nm", "-D", "--defined-only", os.path.join(ROOT, "voxtral.cpp_b200", "libvtx_fa.so")],
+                         capture_output=True, text=True, check=True).stdout
+    exported = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    for s in declared_symbols():
+        assert s in exported, s
+        assert hasattr(lib, s)
+
+
+def test_struct_layouts_match_ctypes(tmp_path):
+    import vtx_attn
+    src = tmp_path / "probe.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vtx_fa.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(vtx_tensor), sizeof(vtx_fa_params),'
+                   ' sizeof(vtx_decode_batch), offsetof(vtx_tensor, data), offsetof(vtx_decode_batch, q),'
+                   ' sizeof(vtx_block_q8_0)); return 0;}\n')
+    exe = tmp_path / "probe"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    assert vals == [ctypes.sizeof(vtx_attn.VtxTensor), ctypes.sizeof(vtx_attn.FaParams),
+                    ctypes.sizeof(vtx_attn.DecodeBatch), vtx_attn.VtxTensor.data.offset,
+                    vtx_attn.DecodeBatch.q.offset, 34]
+
+
+def test_abi_version_and_strerror(lib):
+    assert lib.vtx_abi_version() == 1
+    assert lib.vtx_strerror(0) == b"ok"
+    assert b"workspace" in lib.vtx_strerror(-6)
+
+
+def _t(lib_mod, ttype, ne, nb, ptr=0x1000):
+    t = lib_mod.VtxTensor()
+    t.type = ttype
+    for i in range(4):
+        t.ne[i], t.nb[i] = ne[i], nb[i]
+    t.data = ptr
+    return t
+
+
+def test_validation_without_device(lib):
+    """Rejected operands come back as status codes, no device involved."""
+    import vtx_attn as V
+    D, nq, nkv, Hq, Hkv = 64, 8, 16, 4, 2
+    q = _t(V, V.F32, [D, nq, Hq, 1], [4, 4 * D * Hq, 4 * D, 4 * D * Hq * nq])
+    k = _t(V, V.F16, [D, nkv, Hkv, 1], [2, 2 * D * Hkv, 2 * D, 2 * D * Hkv * nkv])
+    dst = _t(V, V.F32, [D, Hq, nq, 1], [4, 4 * D, 4 * D * Hq, 4 * D * Hq * nq])
+    p = V.params(0.125)
+    B = ctypes.byref
+    assert lib.vtx_flash_attn_ext(None, B(k), B(k), None, B(p), B(dst), None, 0, None) == -1
+    bad = _t(V, 30, k.ne, k.nb)                                  # BF16: not a supported K type
+    assert lib.vtx_flash_attn_ext(B(q), B(bad), B(bad), None, B(p), B(dst), None, 0, None) == -2
+    k3 = _t(V, V.F16, [D, nkv, 3, 1], [2, 2 * D * 3, 2 * D, 2 * D * 3 * nkv])   # 4 % 3 != 0
+    assert lib.vtx_flash_attn_ext(B(q), B(k3), B(k3), None, B(p), B(dst), None, 0, None) == -3
+    q96 = _t(V, V.F32, [96, nq, Hq, 1], [4, 4 * 96 * Hq, 4 * 96, 4 * 96 * Hq * nq])
+    k96 = _t(V, V.F16, [96, nkv, Hkv, 1], [2, 2 * 96 * Hkv, 2 * 96, 2 * 96 * Hkv * nkv])
+    d96 = _t(V, V.F32, [96, Hq, nq, 1], [4, 4 * 96, 4 * 96 * Hq, 4 * 96 * Hq * nq])
+    assert lib.vtx_flash_attn_ext(B(q96), B(k96), B(k96), None, B(p), B(d96), None, 0, None) == -5
+    pw = V.params(0.125, window=10)                              # window without causal
+    assert lib.vtx_flash_attn_ext(B(q), B(k), B(k), None, B(pw), B(dst), None, 0, None) == -5
+    m32 = _t(V, V.F32, [nkv, nq, 1, 1], [4, 4 * nkv, 4 * nkv * nq, 4 * nkv * nq])
+    assert lib.vtx_flash_attn_ext(B(q), B(k), B(k), B(m32), B(p), B(dst), None, 0, None) == -2
+    assert lib.vtx_flash_attn_ext_workspace(B(q96), B(k96), B(k96), B(p)) == ctypes.c_size_t(-1).value
+
+
+def test_workspace_query_is_host_only(lib):
+    import vtx_attn as V
+    D, nq, nkv, Hq, Hkv = 128, 1, 4096, 32, 8
+    q = _t(V, V.F32, [D, nq, Hq, 1], [4, 4 * D * Hq, 4 * D, 4 * D * Hq * nq])
+    k = _t(V, V.F16, [D, nkv, Hkv, 1], [2, 2 * D * Hkv, 2 * D, 2 * D * Hkv * nkv])
+    n = lib.vtx_flash_attn_ext_workspace(ctypes.byref(q), ctypes.byref(k), ctypes.byref(k),
+                                         ctypes.byref(V.params(0.088)))
+    assert 0 < n < (1 << 30)

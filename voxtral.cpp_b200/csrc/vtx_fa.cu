@@ -1,0 +1,573 @@
+// vtx_fa.cu — C ABI entry points (include/vtx_fa.h): operand validation,
+// kernel selection, TMA descriptor encoding and workspace accounting.
+//
+// Path selection for vtx_flash_attn_ext (the ggml_flash_attn_ext node of
+// src/voxtral.cpp:1611 / :1802):
+//   * many query rows (n_q * Hq/Hkv >= 64) and head_dim 64/128
+//       -> fa_prefill_sm100_kernel (tcgen05 + TMEM + TMA).  F16 K/V whose
+//          strides TMA can address are read in place; F32 / Q8_0 / oddly
+//          strided K/V are first converted to a packed f16 copy in the
+//          workspace (what ggml-cuda does for non-F16 caches too).
+//   * otherwise (decode, short chunks) -> fa_splitkv_kernel on the native
+//     K/V dtype + fa_combine_kernel when the keys are split.
+// Nothing here allocates, synchronises or aborts.
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <cuda_fp16.h>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+
+#include "../../include/vtx_fa.h"
+#include "vtx_ptx.cuh"
+#include "fa_splitkv.cuh"
+#include "fa_prefill_sm100.cuh"
+
+using namespace vtx;
+
+// Device-side error word written by bounded waits that ran out (see
+// vtx_ptx.cuh).  One per device, read and cleared by vtx_read_device_error.
+__device__ int g_vtx_kernel_err;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+    int ready = 0;
+    int ok = 0;
+    int sms = 148;
+    int *err = nullptr;
+};
+DeviceState g_dev[kMaxDevices];
+std::mutex g_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+int ensure_device(DeviceState **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VTX_ERR_NO_DEVICE;
+    DeviceState &s = g_dev[dev];
+    if (!s.ready) {
+        std::lock_guard<std::mutex> lk(g_mu);
+        if (!s.ready) {
+            int major = 0, minor = 0;
+            cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+            cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev);
+            s.ok = (major == 10 && minor == 0);
+            void *p = nullptr;
+            if (s.ok && cudaGetSymbolAddress(&p, g_vtx_kernel_err) != cudaSuccess) s.ok = 0;
+            s.err = static_cast<int *>(p);
+            if (s.ok && !g_encode) {
+                cudaDriverEntryPointQueryResult q;
+                void *fn = nullptr;
+                if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+                    q == cudaDriverEntryPointSuccess)
+                    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+            }
+            cudaGetLastError();
+            s.ready = 1;
+        }
+    }
+    if (!s.ok) return VTX_ERR_NO_DEVICE;
+    *out = &s;
+    return VTX_OK;
+}
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline int elem_size(int t) { return t == VTX_TYPE_F32 ? 4 : 2; }
+inline int row_bytes(int t, int64_t d) { return t == VTX_TYPE_Q8_0 ? (int)(d / 32 * 34) : (int)(d * elem_size(t)); }
+
+// ---- operand checks ----------------------------------------------------------
+
+struct Geo {
+    int D, n_q, n_kv, Hq, Hkv, G, B, Bkv;
+    int kv_type;
+};
+
+int check_operands(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, const vtx_tensor *mask,
+                   const vtx_fa_params *p, const vtx_tensor *dst, Geo *g) {
+    if (!q || !k || !v || !p) return VTX_ERR_NULL;
+    if (q->type != VTX_TYPE_F32 && q->type != VTX_TYPE_F16) return VTX_ERR_TYPE;
+    if (k->type != v->type) return VTX_ERR_TYPE;
+    if (k->type != VTX_TYPE_F32 && k->type != VTX_TYPE_F16 && k->type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    for (int i = 0; i < 4; ++i)
+        if (q->ne[i] < 0 || k->ne[i] < 0 || v->ne[i] < 0) return VTX_ERR_SHAPE;
+    if (q->ne[0] != k->ne[0] || v->ne[0] != k->ne[0]) return VTX_ERR_SHAPE;
+    if (k->ne[1] != v->ne[1] || k->ne[2] != v->ne[2] || k->ne[3] != v->ne[3]) return VTX_ERR_SHAPE;
+    if (k->ne[2] == 0 || q->ne[2] % k->ne[2] != 0) return VTX_ERR_SHAPE;
+    if (k->ne[3] == 0 || q->ne[3] % k->ne[3] != 0) return VTX_ERR_SHAPE;
+    const int64_t D = q->ne[0];
+    if (D != 64 && D != 128) return VTX_ERR_UNSUPPORTED;
+    if (q->ne[1] > INT32_MAX || k->ne[1] > INT32_MAX || q->ne[2] > 65535 || q->ne[3] > 65535) return VTX_ERR_SHAPE;
+    if ((size_t)q->nb[0] != (size_t)elem_size(q->type)) return VTX_ERR_STRIDE;
+    if (k->type == VTX_TYPE_Q8_0) {
+        if (k->nb[0] != 34 || v->nb[0] != 34) return VTX_ERR_STRIDE;
+    } else if (k->nb[0] != (size_t)elem_size(k->type) || v->nb[0] != (size_t)elem_size(v->type)) {
+        return VTX_ERR_STRIDE;
+    }
+    if (p->window < 0 || (p->window > 0 && !p->causal)) return VTX_ERR_UNSUPPORTED;
+    if (!std::isfinite(p->scale) || !std::isfinite(p->max_bias) || !std::isfinite(p->logit_softcap))
+        return VTX_ERR_UNSUPPORTED;
+    if (dst) {
+        if (dst->type != VTX_TYPE_F32) return VTX_ERR_TYPE;
+        if (dst->ne[0] != v->ne[0] || dst->ne[1] != q->ne[2] || dst->ne[2] != q->ne[1] || dst->ne[3] != q->ne[3])
+            return VTX_ERR_SHAPE;
+        if (dst->nb[0] != 4 || dst->nb[1] % 16 || dst->nb[2] % 16 || dst->nb[3] % 16) return VTX_ERR_STRIDE;
+    }
+    if (mask) {
+        if (mask->type != VTX_TYPE_F16) return VTX_ERR_TYPE;
+        if (mask->ne[0] < k->ne[1] || mask->ne[1] < q->ne[1]) return VTX_ERR_SHAPE;
+        if (mask->ne[2] <= 0 || mask->ne[3] <= 0 || q->ne[2] % mask->ne[2] || q->ne[3] % mask->ne[3])
+            return VTX_ERR_SHAPE;
+        if (mask->nb[0] != 2) return VTX_ERR_STRIDE;
+    }
+    g->D = (int)D;
+    g->n_q = (int)q->ne[1];
+    g->n_kv = (int)k->ne[1];
+    g->Hq = (int)q->ne[2];
+    g->Hkv = (int)k->ne[2];
+    g->G = g->Hq / g->Hkv;
+    g->B = (int)q->ne[3];
+    g->Bkv = (int)k->ne[3];
+    g->kv_type = k->type;
+    return VTX_OK;
+}
+
+// ---- plans ---------------------------------------------------------------------
+
+struct SplitPlan {
+    int maxr, tok_per_cta, hc, n_hchunks, n_qtiles, chunk, n_splits, tk;
+    size_t part_bytes;     // partial (o, m, l) workspace
+};
+
+int largest_divisor_le(int n, int cap) {
+    for (int d = cap; d >= 1; --d)
+        if (n % d == 0) return d;
+    return 1;
+}
+
+SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched) {
+    SplitPlan s{};
+    s.tk = g.kv_type == VTX_TYPE_F32 ? 32 : 64;
+    s.maxr = (g.n_q * g.G <= 4 && g.G <= 4) ? 4 : 16;
+    s.hc = largest_divisor_le(g.G, s.maxr);
+    s.n_hchunks = g.G / s.hc;
+    s.tok_per_cta = std::max(1, s.maxr / s.hc);
+    s.n_qtiles = (g.n_q + s.tok_per_cta - 1) / s.tok_per_cta;
+    const long long base = (long long)g.B * g.Hkv * s.n_hchunks * s.n_qtiles;
+    const int kv = std::max(1, max_kv);
+    const int max_tiles = (kv + s.tk - 1) / s.tk;
+    long long want = (4LL * sms + base - 1) / base;     // ~4 CTAs per SM in flight
+    if (batched) want = std::max<long long>(want, (kv + 1023) / 1024);
+    int n_splits = (int)std::min<long long>(std::max<long long>(want, 1), max_tiles);
+    int chunk_tiles = (max_tiles + n_splits - 1) / n_splits;
+    s.chunk = chunk_tiles * s.tk;
+    s.n_splits = (kv + s.chunk - 1) / s.chunk;
+    s.part_bytes = 0;
+    if (s.n_splits > 1) {
+        const size_t work = (size_t)base * s.n_splits * s.maxr;
+        s.part_bytes = align_up(work * g.D * 4, 256) + align_up(work * 2 * 4, 256);
+    }
+    return s;
+}
+
+struct PrefillPlan {
+    bool use = false;
+    bool convert = false;      // K/V copied to packed f16 in the workspace
+    int nqt = 1, tok_per_tile = 0, n_tiles_q = 0, n_cta_q = 0;
+    size_t conv_bytes = 0;
+};
+
+bool tma_ok(const vtx_tensor *t) {
+    const uintptr_t base = reinterpret_cast<uintptr_t>(t->data);
+    if (base % 16) return false;
+    for (int i = 1; i < 4; ++i)
+        if (t->ne[i] > 1 && (t->nb[i] % 16 || t->nb[i] >= (1ULL << 40))) return false;
+    return true;
+}
+
+bool q_rows_aligned(const vtx_tensor *q) {
+    const uintptr_t base = reinterpret_cast<uintptr_t>(q->data);
+    if (base % 16) return false;
+    for (int i = 1; i < 4; ++i)
+        if (q->ne[i] > 1 && q->nb[i] % 16) return false;
+    return true;
+}
+
+PrefillPlan plan_prefill(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, int sms) {
+    PrefillPlan p;
+    if (g.G > 128) return p;
+    if ((long long)g.n_q * g.G < 64) return p;
+    if (!q_rows_aligned(q)) return p;
+    p.use = true;
+    p.convert = !(g.kv_type == VTX_TYPE_F16 && tma_ok(k) && tma_ok(v));
+    p.tok_per_tile = 128 / g.G;
+    p.n_tiles_q = (g.n_q + p.tok_per_tile - 1) / p.tok_per_tile;
+    const long long ctas2 = (long long)((p.n_tiles_q + 1) / 2) * g.Hkv * g.B;
+    p.nqt = (p.n_tiles_q >= 2 && ctas2 >= (sms * 3) / 4) ? 2 : 1;
+    p.n_cta_q = (p.n_tiles_q + p.nqt - 1) / p.nqt;
+    if (p.convert) p.conv_bytes = 2 * align_up((size_t)g.Bkv * g.Hkv * g.n_kv * g.D * 2, 256);
+    return p;
+}
+
+// ---- conversion kernel: K/V (F32 | F16 strided | Q8_0) -> packed f16 ---------
+
+__global__ void convert_kv_f16_kernel(const char *src, long long nb1, long long nb2, long long nb3, int type,
+                                      int D, int n_kv, int H, int Bk, __half *dst) {
+    const long long total = (long long)Bk * H * n_kv * D;
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (long long)gridDim.x * blockDim.x) {
+        const int d = (int)(i % D);
+        long long r = i / D;
+        const int t = (int)(r % n_kv); r /= n_kv;
+        const int h = (int)(r % H);
+        const int b = (int)(r / H);
+        const char *row = src + (long long)t * nb1 + (long long)h * nb2 + (long long)b * nb3;
+        float x;
+        if (type == VTX_TYPE_F32) x = reinterpret_cast<const float *>(row)[d];
+        else if (type == VTX_TYPE_F16) x = __half2float(reinterpret_cast<const __half *>(row)[d]);
+        else {
+            const char *blk = row + (d / 32) * 34;
+            x = __half2float(*reinterpret_cast<const __half *>(blk)) * (float)(int8_t)blk[2 + d % 32];
+        }
+        dst[i] = __float2half_rn(x);
+    }
+}
+
+int encode_kv_map(CUtensorMap *m, const void *ptr, int D, int n_kv, int H, int Bk, size_t nb1, size_t nb2,
+                  size_t nb3) {
+    if (!g_encode) return VTX_ERR_CUDA;
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)n_kv, (cuuint64_t)H, (cuuint64_t)Bk};
+    cuuint64_t strides[3] = {(cuuint64_t)nb1, (cuuint64_t)(H > 1 ? nb2 : nb1 * (size_t)n_kv),
+                             (cuuint64_t)(Bk > 1 ? nb3 : (H > 1 ? nb2 : nb1 * (size_t)n_kv) * (size_t)H)};
+    for (int i = 0; i < 3; ++i)
+        if (strides[i] % 16 || strides[i] == 0) return VTX_ERR_STRIDE;
+    cuuint32_t box[4] = {64, 128, 1, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
+}
+
+void fill_math(float scale, float max_bias, float softcap, int Hq, float *qk_scale, float *softcap_out, float *m0,
+               float *m1, int *n_head_log2) {
+    *n_head_log2 = 1 << (int)std::floor(std::log2((double)Hq));
+    *m0 = std::pow(2.0f, -(max_bias) / (float)*n_head_log2);
+    *m1 = std::pow(2.0f, -(max_bias / 2.0f) / (float)*n_head_log2);
+    *softcap_out = softcap;
+    *qk_scale = softcap != 0.0f ? scale / softcap : scale;
+}
+
+template <int D, int KVT, int MAXR>
+int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
+    constexpr int smem = splitkv_smem_bytes<D, KVT, MAXR>();
+    static int attr_done[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(fa_splitkv_kernel<D, KVT, MAXR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev] = 1;
+    }
+    fa_splitkv_kernel<D, KVT, MAXR><<<grid, 128, smem, st>>>(a);
+    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (!a.write_final) {
+        const long long rows = (long long)a.B * grid.y * a.n_qtiles * a.tok_per_cta * a.hc;
+        fa_combine_kernel<D, MAXR><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, (int)grid.y);
+        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    }
+    return VTX_OK;
+}
+
+template <int D, int KVT>
+int launch_split_d(const SplitArgs &a, int maxr, dim3 grid, cudaStream_t st) {
+    return maxr == 4 ? launch_split_t<D, KVT, 4>(a, grid, st) : launch_split_t<D, KVT, 16>(a, grid, st);
+}
+
+int launch_split(const SplitArgs &a, int D, int kvt, int maxr, dim3 grid, cudaStream_t st) {
+    if (D == 64) {
+        if (kvt == VTX_TYPE_F16) return launch_split_d<64, 1>(a, maxr, grid, st);
+        if (kvt == VTX_TYPE_F32) return launch_split_d<64, 0>(a, maxr, grid, st);
+        return launch_split_d<64, 8>(a, maxr, grid, st);
+    }
+    if (kvt == VTX_TYPE_F16) return launch_split_d<128, 1>(a, maxr, grid, st);
+    if (kvt == VTX_TYPE_F32) return launch_split_d<128, 0>(a, maxr, grid, st);
+    return launch_split_d<128, 8>(a, maxr, grid, st);
+}
+
+int pick_vec(int row, std::initializer_list<unsigned long long> vals) {
+    for (int v : {16, 8, 4}) {
+        if (row % v) continue;
+        bool ok = true;
+        for (auto x : vals)
+            if (x % (unsigned long long)v) { ok = false; break; }
+        if (ok) return v;
+    }
+    return 0;
+}
+
+template <int D, int NQT, bool HM>
+int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const PrefillArgs &a, dim3 grid,
+                     cudaStream_t st) {
+    using C = PrefillCfg<D, NQT>;
+    static int attr_done[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM) != cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev] = 1;
+    }
+    fa_prefill_sm100_kernel<D, NQT, HM><<<grid, C::NTHREADS, C::SMEM, st>>>(mk, mv, a);
+    return cudaGetLastError() == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
+}
+
+int launch_prefill(int D, int nqt, bool hm, const CUtensorMap &mk, const CUtensorMap &mv, const PrefillArgs &a,
+                   dim3 grid, cudaStream_t st) {
+    if (D == 64) {
+        if (nqt == 2) return hm ? launch_prefill_t<64, 2, true>(mk, mv, a, grid, st) : launch_prefill_t<64, 2, false>(mk, mv, a, grid, st);
+        return hm ? launch_prefill_t<64, 1, true>(mk, mv, a, grid, st) : launch_prefill_t<64, 1, false>(mk, mv, a, grid, st);
+    }
+    if (nqt == 2) return hm ? launch_prefill_t<128, 2, true>(mk, mv, a, grid, st) : launch_prefill_t<128, 2, false>(mk, mv, a, grid, st);
+    return hm ? launch_prefill_t<128, 1, true>(mk, mv, a, grid, st) : launch_prefill_t<128, 1, false>(mk, mv, a, grid, st);
+}
+
+size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, int sms) {
+    if (g.n_q == 0) return 0;
+    const PrefillPlan pp = plan_prefill(g, q, k, v, sms);
+    if (pp.use) return pp.conv_bytes;
+    return plan_split(g, sms, g.n_kv, false).part_bytes;
+}
+
+}  // namespace
+
+// ================================================================================
+extern "C" {
+
+const char *vtx_strerror(int status) {
+    switch (status) {
+        case VTX_OK: return "ok";
+        case VTX_ERR_NULL: return "required pointer is NULL";
+        case VTX_ERR_TYPE: return "unsupported or mismatched tensor type";
+        case VTX_ERR_SHAPE: return "inconsistent tensor shapes";
+        case VTX_ERR_STRIDE: return "unsupported stride or alignment";
+        case VTX_ERR_UNSUPPORTED: return "unsupported head_dim or parameter";
+        case VTX_ERR_WORKSPACE: return "workspace too small or misaligned";
+        case VTX_ERR_CUDA: return "CUDA launch or runtime call failed";
+        case VTX_ERR_NO_DEVICE: return "no sm_100 device is current";
+        default: return "unknown status";
+    }
+}
+
+int vtx_abi_version(void) { return VTX_FA_ABI_VERSION; }
+
+size_t vtx_flash_attn_ext_workspace(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v,
+                                    const vtx_fa_params *params) {
+    Geo g;
+    if (check_operands(q, k, v, nullptr, params, nullptr, &g) != VTX_OK) return (size_t)-1;
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+    return workspace_for(g, q, k, v, sms);
+}
+
+int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, const vtx_tensor *mask,
+                       const vtx_fa_params *params, vtx_tensor *dst, void *workspace, size_t workspace_bytes,
+                       void *stream) {
+    if (!dst) return VTX_ERR_NULL;
+    Geo g;
+    int rc = check_operands(q, k, v, mask, params, dst, &g);
+    if (rc != VTX_OK) return rc;
+    if ((g.n_q > 0 && g.n_kv > 0) && (!q->data || !k->data || !v->data || !dst->data)) return VTX_ERR_NULL;
+    if (mask && !mask->data) return VTX_ERR_NULL;
+    if (reinterpret_cast<uintptr_t>(dst->data) % 16) return VTX_ERR_STRIDE;
+    DeviceState *ds = nullptr;
+    rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    if (g.n_q == 0 || g.B == 0 || g.Hq == 0) return VTX_OK;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (workspace_bytes < workspace_for(g, q, k, v, ds->sms)) return VTX_ERR_WORKSPACE;
+    if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
+
+    float qk_scale, softcap, m0, m1;
+    int nhl2;
+    fill_math(params->scale, params->max_bias, params->logit_softcap, g.Hq, &qk_scale, &softcap, &m0, &m1, &nhl2);
+
+    const PrefillPlan pp = plan_prefill(g, q, k, v, ds->sms);
+    if (pp.use && g.n_kv > 0) {
+        const void *kp = k->data, *vp = v->data;
+        size_t knb1 = k->nb[1], knb2 = k->nb[2], knb3 = k->nb[3];
+        size_t vnb1 = v->nb[1], vnb2 = v->nb[2], vnb3 = v->nb[3];
+        if (pp.convert) {
+            __half *kc = static_cast<__half *>(workspace);
+            __half *vc = reinterpret_cast<__half *>(static_cast<char *>(workspace) + pp.conv_bytes / 2);
+            const long long total = (long long)g.Bkv * g.Hkv * g.n_kv * g.D;
+            const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * ds->sms);
+            convert_kv_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const char *>(k->data), k->nb[1], k->nb[2],
+                                                          k->nb[3], k->type, g.D, g.n_kv, g.Hkv, g.Bkv, kc);
+            convert_kv_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const char *>(v->data), v->nb[1], v->nb[2],
+                                                          v->nb[3], v->type, g.D, g.n_kv, g.Hkv, g.Bkv, vc);
+            if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+            kp = kc;
+            vp = vc;
+            knb1 = vnb1 = (size_t)g.D * 2;
+            knb2 = vnb2 = knb1 * g.n_kv;
+            knb3 = vnb3 = knb2 * g.Hkv;
+        }
+        CUtensorMap mk, mv;
+        rc = encode_kv_map(&mk, kp, g.D, g.n_kv, g.Hkv, g.Bkv, knb1, knb2, knb3);
+        if (rc != VTX_OK) return rc;
+        rc = encode_kv_map(&mv, vp, g.D, g.n_kv, g.Hkv, g.Bkv, vnb1, vnb2, vnb3);
+        if (rc != VTX_OK) return rc;
+        PrefillArgs a{};
+        a.q = static_cast<const char *>(q->data);
+        a.q_f16 = q->type == VTX_TYPE_F16;
+        a.q_nb1 = (long long)q->nb[1]; a.q_nb2 = (long long)q->nb[2]; a.q_nb3 = (long long)q->nb[3];
+        if (mask) {
+            a.mask = static_cast<const char *>(mask->data);
+            a.m_nb1 = (long long)mask->nb[1]; a.m_nb2 = (long long)mask->nb[2]; a.m_nb3 = (long long)mask->nb[3];
+            a.m_ne2 = (int)mask->ne[2]; a.m_ne3 = (int)mask->ne[3];
+        }
+        a.dst = static_cast<char *>(dst->data);
+        a.d_nb1 = (long long)dst->nb[1]; a.d_nb2 = (long long)dst->nb[2]; a.d_nb3 = (long long)dst->nb[3];
+        a.n_q = g.n_q; a.n_kv = g.n_kv; a.Hq = g.Hq; a.Hkv = g.Hkv; a.G = g.G; a.B = g.B;
+        a.tok_per_tile = pp.tok_per_tile; a.n_tiles_q = pp.n_tiles_q; a.n_cta_q = pp.n_cta_q;
+        a.kv_bdiv = g.B / g.Bkv;
+        a.qk_scale_log2 = params->scale * kLog2e;
+        a.qk_scale = qk_scale; a.softcap = softcap;
+        a.max_bias = params->max_bias; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
+        a.causal = params->causal; a.window = params->window;
+        a.q_quant8 = g.kv_type == VTX_TYPE_Q8_0;
+        a.err = ds->err;
+        dim3 grid(pp.n_cta_q, g.Hkv, g.B);
+        return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, a, grid, st);
+    }
+
+    // ---- split-KV path ---------------------------------------------------------
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, false);
+    SplitArgs a{};
+    a.q = static_cast<const char *>(q->data);
+    a.q_f16 = q->type == VTX_TYPE_F16;
+    a.q_nb1 = (long long)q->nb[1]; a.q_nb2 = (long long)q->nb[2]; a.q_nb3 = (long long)q->nb[3];
+    a.k = static_cast<const char *>(k->data); a.v = static_cast<const char *>(v->data);
+    a.k_nb1 = (long long)k->nb[1]; a.k_nb2 = (long long)k->nb[2]; a.k_nb3 = (long long)k->nb[3];
+    a.v_nb1 = (long long)v->nb[1]; a.v_nb2 = (long long)v->nb[2]; a.v_nb3 = (long long)v->nb[3];
+    a.k_bdiv = g.B / g.Bkv; a.v_bdiv = g.B / g.Bkv;
+    a.n_kv = g.n_kv;
+    if (mask) {
+        a.mask = static_cast<const char *>(mask->data);
+        a.m_nb1 = (long long)mask->nb[1]; a.m_nb2 = (long long)mask->nb[2]; a.m_nb3 = (long long)mask->nb[3];
+        a.m_ne2 = (int)mask->ne[2]; a.m_ne3 = (int)mask->ne[3];
+    }
+    a.dst = static_cast<char *>(dst->data);
+    a.d_nb1 = (long long)dst->nb[1]; a.d_nb2 = (long long)dst->nb[2]; a.d_nb3 = (long long)dst->nb[3];
+    a.n_q = g.n_q; a.Hq = g.Hq; a.Hkv = g.Hkv; a.G = g.G; a.B = g.B;
+    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
+    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
+    a.qk_scale = qk_scale; a.softcap = softcap; a.max_bias = params->max_bias; a.m0 = m0; a.m1 = m1;
+    a.n_head_log2 = nhl2;
+    a.causal = params->causal; a.window = params->window;
+    a.write_final = sp.n_splits <= 1;
+    if (!a.write_final) {
+        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
+        a.part_o = static_cast<float *>(workspace);
+        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + align_up(work * g.D * 4, 256));
+    }
+    const int rb = row_bytes(g.kv_type, g.D);
+    a.vec = pick_vec(rb, {reinterpret_cast<uintptr_t>(k->data), reinterpret_cast<uintptr_t>(v->data),
+                          (unsigned long long)k->nb[1], (unsigned long long)(g.Hkv > 1 ? k->nb[2] : 0),
+                          (unsigned long long)(g.Bkv > 1 ? k->nb[3] : 0), (unsigned long long)v->nb[1],
+                          (unsigned long long)(g.Hkv > 1 ? v->nb[2] : 0),
+                          (unsigned long long)(g.Bkv > 1 ? v->nb[3] : 0)});
+    if (!a.vec) return VTX_ERR_STRIDE;
+    a.err = ds->err;
+    dim3 grid((unsigned)(sp.n_splits * sp.n_qtiles), (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)g.B);
+    return launch_split(a, g.D, g.kv_type, sp.maxr, grid, st);
+}
+
+size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *b) {
+    if (!b || b->n_seq < 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv) return (size_t)-1;
+    if (b->head_dim != 64 && b->head_dim != 128) return (size_t)-1;
+    Geo g{b->head_dim, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv,
+          b->n_seq, b->n_seq, b->kv_type};
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+    return plan_split(g, sms, g.n_kv, true).part_bytes;
+}
+
+int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, size_t workspace_bytes, void *stream) {
+    if (!b) return VTX_ERR_NULL;
+    if (b->n_seq < 0 || b->n_head_q <= 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv || b->max_kv_len < 0)
+        return VTX_ERR_SHAPE;
+    if (b->head_dim != 64 && b->head_dim != 128) return VTX_ERR_UNSUPPORTED;
+    if (b->kv_type != VTX_TYPE_F16 && b->kv_type != VTX_TYPE_F32 && b->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    if (b->n_seq == 0) return VTX_OK;
+    if (!b->q || !b->k_ptrs || !b->v_ptrs || !b->kv_len || !b->dst) return VTX_ERR_NULL;
+    if (b->n_seq > 65535 || b->n_head_q / b->n_head_kv > 16) return VTX_ERR_UNSUPPORTED;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    const int D = b->head_dim;
+    Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
+          b->n_seq, b->kv_type};
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true);
+    if (workspace_bytes < sp.part_bytes) return VTX_ERR_WORKSPACE;
+    if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
+    SplitArgs a{};
+    a.q = reinterpret_cast<const char *>(b->q);
+    a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
+    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len;
+    a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
+    a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
+    a.k_bdiv = a.v_bdiv = 1;
+    a.n_kv = g.n_kv;
+    a.dst = reinterpret_cast<char *>(b->dst);
+    a.d_nb1 = (long long)D * 4; a.d_nb2 = (long long)b->n_head_q * D * 4; a.d_nb3 = (long long)b->n_head_q * D * 4;
+    a.n_q = 1; a.Hq = b->n_head_q; a.Hkv = b->n_head_kv; a.G = g.G; a.B = b->n_seq;
+    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
+    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
+    float qk_scale, softcap, m0, m1;
+    int nhl2;
+    fill_math(b->scale, 0.0f, 0.0f, b->n_head_q, &qk_scale, &softcap, &m0, &m1, &nhl2);
+    a.qk_scale = qk_scale; a.softcap = 0.0f; a.max_bias = 0.0f; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
+    a.write_final = sp.n_splits <= 1;
+    if (!a.write_final) {
+        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
+        a.part_o = static_cast<float *>(workspace);
+        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + align_up(work * D * 4, 256));
+    }
+    const int rb = row_bytes(b->kv_type, D);
+    a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
+    // stream base pointers are only known on the device: require 16-byte
+    // aligned bases whenever the strides allow 16-byte copies
+    if (!a.vec) return VTX_ERR_STRIDE;
+    a.err = ds->err;
+    dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
+    return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
+}
+
+int vtx_read_device_error(void *stream) {
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    int h = 0;
+    if (cudaMemcpyFromSymbolAsync(&h, g_vtx_kernel_err, sizeof(int), 0, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+        return VTX_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return VTX_ERR_CUDA;
+    const int zero = 0;
+    if (cudaMemcpyToSymbolAsync(g_vtx_kernel_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st) != cudaSuccess)
+        return VTX_ERR_CUDA;
+    if (cudaStreamSynchronize(st) != cudaSuccess) return VTX_ERR_CUDA;
+    return h;
+}
+
+}  // extern "C"

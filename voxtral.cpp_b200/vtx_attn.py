@@ -1,0 +1,245 @@
+"""Host-side mirror of ggml_flash_attn_ext over the libvtx_fa.so C ABI.
+
+This is the Python face of the node voxtral.cpp builds at src/voxtral.cpp:1611
+(encoder) and src/voxtral.cpp:1802 (decoder): same operands, same argument
+meaning (ggml views [D, n, H, B] -> here torch tensors (B, H, n, D) with any
+strides), same result layout (ggml dst [Dv, Hq, n_q, B] -> torch (B, n_q, Hq,
+Dv) float32).  Errors from the library raise ``VtxError`` (ggml would abort
+with GGML_ASSERT).  torch supplies device memory and streams only; all
+arithmetic runs in the library's sm_100a kernels.  There is no CPU fallback:
+without the library or an sm_100 device every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from typing import Optional, Sequence
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "libvtx_fa.so")
+
+F32, F16, Q8_0 = 0, 1, 8
+QK8_0, Q8_0_BLOCK = 32, 34
+
+STATUS = {0: "ok", -1: "null pointer", -2: "type", -3: "shape", -4: "stride", -5: "unsupported",
+          -6: "workspace", -7: "cuda", -8: "no sm_100 device"}
+
+
+class VtxError(RuntimeError):
+    def __init__(self, status: int, what: str = ""):
+        self.status = status
+        super().__init__(f"vtx status {status} ({STATUS.get(status, '?')}){': ' + what if what else ''}")
+
+
+class VtxTensor(ctypes.Structure):
+    _fields_ = [("type", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("ne", ctypes.c_int64 * 4), ("nb", ctypes.c_size_t * 4),
+                ("data", ctypes.c_void_p)]
+
+
+class FaParams(ctypes.Structure):
+    _fields_ = [("scale", ctypes.c_float), ("max_bias", ctypes.c_float),
+                ("logit_softcap", ctypes.c_float), ("causal", ctypes.c_int32),
+                ("window", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
+class DecodeBatch(ctypes.Structure):
+    _fields_ = [("n_seq", ctypes.c_int32), ("n_head_q", ctypes.c_int32),
+                ("n_head_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("kv_type", ctypes.c_int32), ("max_kv_len", ctypes.c_int32),
+                ("kv_nb1", ctypes.c_size_t), ("kv_nb2", ctypes.c_size_t),
+                ("q", ctypes.c_void_p), ("k_ptrs", ctypes.c_void_p),
+                ("v_ptrs", ctypes.c_void_p), ("kv_len", ctypes.c_void_p),
+                ("dst", ctypes.c_void_p), ("scale", ctypes.c_float),
+                ("reserved", ctypes.c_int32)]
+
+
+_lib = None
+
+
+def load(path: str = LIB_PATH):
+    """Load libvtx_fa.so (built by build.py).  Raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise RuntimeError(f"libvtx_fa.so not built ({path}); run voxtral.cpp_b200/build.py")
+    L = ctypes.CDLL(path)
+    P = ctypes.POINTER
+    L.vtx_flash_attn_ext.argtypes = [P(VtxTensor), P(VtxTensor), P(VtxTensor), P(VtxTensor),
+                                     P(FaParams), P(VtxTensor), ctypes.c_void_p, ctypes.c_size_t,
+                                     ctypes.c_void_p]
+    L.vtx_flash_attn_ext.restype = ctypes.c_int
+    L.vtx_flash_attn_ext_workspace.argtypes = [P(VtxTensor), P(VtxTensor), P(VtxTensor), P(FaParams)]
+    L.vtx_flash_attn_ext_workspace.restype = ctypes.c_size_t
+    L.vtx_flash_attn_decode_batched.argtypes = [P(DecodeBatch), ctypes.c_void_p, ctypes.c_size_t,
+                                                ctypes.c_void_p]
+    L.vtx_flash_attn_decode_batched.restype = ctypes.c_int
+    L.vtx_flash_attn_decode_batched_workspace.argtypes = [P(DecodeBatch)]
+    L.vtx_flash_attn_decode_batched_workspace.restype = ctypes.c_size_t
+    L.vtx_read_device_error.argtypes = [ctypes.c_void_p]
+    L.vtx_read_device_error.restype = ctypes.c_int
+    L.vtx_strerror.argtypes = [ctypes.c_int]
+    L.vtx_strerror.restype = ctypes.c_char_p
+    L.vtx_abi_version.argtypes = []
+    L.vtx_abi_version.restype = ctypes.c_int
+    _lib = L
+    return L
+
+
+def _ggml_type(t: torch.Tensor, kv_type: Optional[int]) -> int:
+    if kv_type is not None:
+        return kv_type
+    if t.dtype == torch.float32:
+        return F32
+    if t.dtype == torch.float16:
+        return F16
+    raise VtxError(-2, f"dtype {t.dtype}")
+
+
+def desc(t: Optional[torch.Tensor], ttype: Optional[int] = None) -> Optional[VtxTensor]:
+    """ggml descriptor of a torch view: shape (B, H, n, D) -> ne [D, n, H, B].
+    Q8_0 tensors are uint8 with the last axis holding D/32 blocks of 34 bytes."""
+    if t is None:
+        return None
+    if t.dim() > 4:
+        raise VtxError(-3, "at most 4 dims")
+    ttype = _ggml_type(t, ttype)
+    shape = [1] * (4 - t.dim()) + list(t.shape)
+    es = t.element_size()
+    strides = [0] * (4 - t.dim()) + [s * es for s in t.stride()]
+    ne = list(reversed(shape))
+    nb = list(reversed(strides))
+    if ttype == Q8_0:
+        ne[0] = ne[0] // Q8_0_BLOCK * QK8_0
+        nb[0] = Q8_0_BLOCK
+    row = nb[0] * (ne[0] // QK8_0 if ttype == Q8_0 else ne[0])
+    for i in range(1, 4):
+        if nb[i] == 0 or ne[i] == 1:
+            nb[i] = nb[i] or (row if i == 1 else nb[i - 1] * ne[i - 1])
+    d = VtxTensor()
+    d.type = ttype
+    for i in range(4):
+        d.ne[i] = ne[i]
+        d.nb[i] = nb[i]
+    d.data = t.data_ptr()
+    return d
+
+
+def params(scale: float, max_bias: float = 0.0, logit_softcap: float = 0.0,
+           causal: bool = False, window: int = 0) -> FaParams:
+    p = FaParams()
+    p.scale, p.max_bias, p.logit_softcap = float(scale), float(max_bias), float(logit_softcap)
+    p.causal, p.window = int(bool(causal)), int(window)
+    return p
+
+
+def _check(rc: int, what: str = "") -> None:
+    if rc != 0:
+        raise VtxError(rc, what)
+
+
+def workspace_bytes(q, k, v, scale, max_bias=0.0, logit_softcap=0.0, causal=False, window=0,
+                    kv_type=None) -> int:
+    L = load()
+    p = params(scale, max_bias, logit_softcap, causal, window)
+    n = L.vtx_flash_attn_ext_workspace(ctypes.byref(desc(q)), ctypes.byref(desc(k, kv_type)),
+                                       ctypes.byref(desc(v, kv_type)), ctypes.byref(p))
+    if n == ctypes.c_size_t(-1).value:
+        raise VtxError(-3, "operands rejected")
+    return int(n)
+
+
+def flash_attn_ext(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                   mask: Optional[torch.Tensor] = None, scale: float = 1.0,
+                   max_bias: float = 0.0, logit_softcap: float = 0.0, *,
+                   causal: bool = False, window: int = 0, kv_type: Optional[int] = None,
+                   out: Optional[torch.Tensor] = None, workspace: Optional[torch.Tensor] = None,
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """ggml_flash_attn_ext(ctx, q, k, v, mask, scale, max_bias, logit_softcap).
+
+    q: (B, Hq, n_q, D) F32/F16 view; k, v: (B, Hkv, n_kv, D) F16/F32 or Q8_0
+    bytes (kv_type=Q8_0); mask: (n_q', n_kv) / (B|1, Hq|1, n_q', n_kv) F16 or
+    None.  Returns (B, n_q, Hq, D) float32 (ggml's permuted dst)."""
+    L = load()
+    B, Hq, n_q = q.shape[0], q.shape[1], q.shape[2]
+    Dv = v.shape[-1] if (kv_type or _ggml_type(v, None)) != Q8_0 else v.shape[-1] // Q8_0_BLOCK * QK8_0
+    if out is None:
+        out = torch.empty((B, n_q, Hq, Dv), dtype=torch.float32, device=q.device)
+    p = params(scale, max_bias, logit_softcap, causal, window)
+    dq, dk, dv = desc(q), desc(k, kv_type), desc(v, kv_type)
+    need = L.vtx_flash_attn_ext_workspace(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv), ctypes.byref(p))
+    if need == ctypes.c_size_t(-1).value:
+        raise VtxError(-3, "operands rejected")
+    if need and (workspace is None or workspace.numel() * workspace.element_size() < need):
+        workspace = torch.empty(need, dtype=torch.uint8, device=q.device)
+    ws_ptr = workspace.data_ptr() if (workspace is not None and need) else None
+    ws_len = workspace.numel() * workspace.element_size() if (workspace is not None and need) else 0
+    dm = desc(mask, F16) if mask is not None else None
+    s = stream if stream is not None else torch.cuda.current_stream(q.device)
+    rc = L.vtx_flash_attn_ext(ctypes.byref(dq), ctypes.byref(dk), ctypes.byref(dv),
+                              ctypes.byref(dm) if dm is not None else None, ctypes.byref(p),
+                              ctypes.byref(desc(out)), ws_ptr, ws_len, ctypes.c_void_p(s.cuda_stream))
+    _check(rc, "vtx_flash_attn_ext")
+    return out
+
+
+class DecodeBatchPlan:
+    """Device-side arrays for vtx_flash_attn_decode_batched over a fixed set of
+    per-stream KV buffers (pointer arrays live on the device so one call can be
+    captured in a CUDA graph and replayed)."""
+
+    def __init__(self, k_bufs: Sequence[torch.Tensor], v_bufs: Sequence[torch.Tensor],
+                 kv_len: torch.Tensor, n_head_q: int, n_head_kv: int, head_dim: int, kv_type: int,
+                 kv_nb1: int, kv_nb2: int, max_kv_len: int, scale: float):
+        dev = kv_len.device
+        self.k_ptrs = torch.tensor([t.data_ptr() for t in k_bufs], dtype=torch.int64, device=dev)
+        self.v_ptrs = torch.tensor([t.data_ptr() for t in v_bufs], dtype=torch.int64, device=dev)
+        self.kv_len = kv_len.to(torch.int32)
+        self.keep = (list(k_bufs), list(v_bufs))
+        b = DecodeBatch()
+        b.n_seq, b.n_head_q, b.n_head_kv, b.head_dim = len(k_bufs), n_head_q, n_head_kv, head_dim
+        b.kv_type, b.max_kv_len, b.kv_nb1, b.kv_nb2 = kv_type, max_kv_len, kv_nb1, kv_nb2
+        b.k_ptrs, b.v_ptrs, b.kv_len = self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(), self.kv_len.data_ptr()
+        b.scale = scale
+        self.batch = b
+        need = load().vtx_flash_attn_decode_batched_workspace(ctypes.byref(b))
+        if need == ctypes.c_size_t(-1).value:
+            raise VtxError(-3, "batch rejected")
+        self.workspace = torch.empty(max(int(need), 1), dtype=torch.uint8, device=dev)
+        self.need = int(need)
+
+    def __call__(self, q: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        if out is None:
+            out = torch.empty_like(q, dtype=torch.float32)
+        self.batch.q = q.data_ptr()
+        self.batch.dst = out.data_ptr()
+        s = stream if stream is not None else torch.cuda.current_stream(q.device)
+        rc = load().vtx_flash_attn_decode_batched(ctypes.byref(self.batch), self.workspace.data_ptr(),
+                                                  self.workspace.numel(), ctypes.c_void_p(s.cuda_stream))
+        _check(rc, "vtx_flash_attn_decode_batched")
+        return out
+
+
+def read_device_error(stream: Optional[torch.cuda.Stream] = None) -> int:
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return int(load().vtx_read_device_error(ctypes.c_void_p(s.cuda_stream)))
+
+
+# ---- reference masks and formats (the shapes voxtral.cpp builds) -----------
+
+def causal_mask(n: int, device=None) -> torch.Tensor:
+    """src/voxtral.cpp:2103-2111 fill_causal_mask -> F16 (:1801)."""
+    m = torch.full((n, n), float("-inf"), device=device).triu(1)
+    return m.to(torch.float16)
+
+
+def window_mask(n: int, window: int = 750, device=None) -> torch.Tensor:
+    """src/voxtral.cpp:2181-2188 chunk-local sliding causal mask -> F16."""
+    qi = torch.arange(n, device=device)[:, None]
+    kj = torch.arange(n, device=device)[None, :]
+    allow = (kj <= qi) & (kj >= (qi - (window - 1)).clamp(min=0))
+    return torch.where(allow, 0.0, float("-inf")).to(torch.float16)
