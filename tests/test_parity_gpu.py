@@ -40,7 +40,15 @@ def check(c, what):
     got = run_gpu(c)
     ref = oracle_out(c)
     assert_close(got, ref, what + " vs ggml-mode oracle")
-    assert_close(got, oracle_out(c, O.MODE_FP64), what + " vs fp64")
+    truth = oracle_out(c, O.MODE_FP64)
+    if c.kv_type == O.Q8_0:
+        # ggml quantizes Q to Q8_0 for a Q8_0 K (and so do the kernels); the
+        # distance to fp64 truth is then bounded by ggml's own, not by 2e-3.
+        own = float(np.max(np.abs(ref.astype(np.float64) - truth)))
+        err = float(np.max(np.abs(got.astype(np.float64) - truth)))
+        assert err <= 1.5 * own + 2e-3, f"{what}: gpu-vs-fp64 {err:.3e}, ggml-vs-fp64 {own:.3e}"
+    else:
+        assert_close(got, truth, what + " vs fp64")
 
 
 # ---- BASELINE configs at parity-test sizes ---------------------------------

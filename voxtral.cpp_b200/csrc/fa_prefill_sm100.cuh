@@ -275,7 +275,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 for (int i = 0; i < 32; ++i) pk[i] = pack_half2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
                 tmem_st32(s_addr + c * 32, pk);
             }
-            if (rescale) {
+            // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
+            // rescales if any of its rows needs it (alpha == 1 for the others).
+            if (__any_sync(0xffffffffu, rescale)) {
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
@@ -321,10 +323,12 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         // =================== TMA producer =====================================
         if (lane == 0) {
             const int bkv = b / a.kv_bdiv;
+            int issued = 0;
             for (int it = 0; it < n_iter; ++it) {
                 const int st = it % C::STAGES;
                 if (it >= C::STAGES &&
                     !mbar_wait(&kv_empty[st], ((it / C::STAGES) - 1) & 1, a.err, VTX_KERR_KV)) break;
+                issued = it + 1;
                 const int y = (j_begin + it) * C::BN;
                 char *ks = smem + C::K_OFF + st * C::TILE_BYTES;
                 char *vs = smem + C::V_OFF + st * C::TILE_BYTES;
@@ -334,6 +338,13 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
 #pragma unroll
                 for (int sub = 0; sub < C::SUB; ++sub) tma_load_4d(vs + sub * 16384, &tmV, &v_full[st], sub * 64, y, g, bkv);
+            }
+            // Drain: the last STAGES loads must have landed before this CTA's
+            // shared memory can be released (already true unless a wait failed).
+            for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it) {
+                const int st = it % C::STAGES;
+                mbar_wait(&k_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
+                mbar_wait(&v_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
             }
         }
     } else {
@@ -384,6 +395,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 if (it > 0) mma_commit(&kv_empty[pst]);
             }
             mma_commit(o_full);
+            // every MMA of this CTA must be retired before TMEM is released
+            mbar_wait(o_full, 0, a.err, VTX_KERR_O);
         }
     }
 

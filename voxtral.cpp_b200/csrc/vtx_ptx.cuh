@@ -1,13 +1,13 @@
 // vtx_ptx.cuh — thin inline-PTX wrappers for sm_100a: mbarriers, TMA tensor
 // loads, tcgen05 (TMEM alloc / MMA / commit / ld / st) and fences.
-// Every wait loop here is bounded: after VTX_SPIN_LIMIT polls it records an
-// error word and returns false instead of hanging the GPU.
+// Every wait loop here is bounded: after VTX_WAIT_NS of wall time it records
+// an error word and returns false instead of hanging the GPU.
 #pragma once
 #include <cstdint>
 #include <cuda_fp16.h>
 
-#ifndef VTX_SPIN_LIMIT
-#define VTX_SPIN_LIMIT (1u << 26)   // ~ >1 s of polling with nanosleep back-off
+#ifndef VTX_WAIT_NS
+#define VTX_WAIT_NS 2000000000ull   // 2 s: far beyond any legitimate pipeline wait
 #endif
 
 namespace vtx {
@@ -46,13 +46,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t phase) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait on parity `phase`.  On timeout sets *err (if given) and
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+// Bounded wait on parity `phase`: gives up after VTX_WAIT_NS of wall time
+// (try_wait may itself suspend for a system-dependent slice, so the bound is
+// on %globaltimer, not on a poll count).  On timeout sets *err (if given) and
 // returns false; the caller must then stop issuing work that depends on it.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *err, int code) {
     if (mbar_try_wait(bar, phase)) return true;
-    for (uint32_t i = 0; i < VTX_SPIN_LIMIT; ++i) {
+    const uint64_t t0 = globaltimer_ns();
+    for (;;) {
         if (mbar_try_wait(bar, phase)) return true;
-        if (i > 64) __nanosleep(32);
+        if (globaltimer_ns() - t0 > VTX_WAIT_NS) break;
     }
     if (err) atomicCAS(err, 0, code);
     return false;
