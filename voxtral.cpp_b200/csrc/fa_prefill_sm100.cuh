@@ -5,17 +5,22 @@
 // (src/voxtral.cpp:1802: GQA 32/8, head_dim 128, causal) are compute-bound.
 // One CTA owns NQT 128-row Q tiles of one KV head (GQA: the G query heads of
 // the group are packed into the rows, row = token * G + head-in-group, so
-// every K/V tile feeds all of them) and walks the key tiles:
+// every K/V tile feeds all of them) and walks the key tiles.  Warp roles, one
+// warpgroup per Q tile plus one producer warpgroup:
 //
-//   warp 4*NQT      TMA producer: K_j, V_j (128 keys x D, 128-byte swizzle)
+//   WG t < NQT      softmax of Q tile t, one thread per row (= TMEM lane):
+//                   tcgen05.ld S, max, P = 2^(x*c - m) (MUFU ex2 for most
+//                   columns, a degree-3 polynomial on the FMA pipe for the
+//                   rest), lazy rescaling (only when the row max grows by more
+//                   than 2^8), P packed to half into the S columns of TMEM.
+//   WG NQT warp 0   TMA producer: K_j, V_j (128 keys x D, 128-byte swizzle)
 //                   into a STAGES-deep shared-memory ring (mbarrier tx count)
-//   warp 4*NQT+1    MMA issuer (one thread): S_t = Q_t K_j^T  (SS, f16->f32,
+//   WG NQT warp 1   MMA issuer (one thread): S_t = Q_t K_j^T  (SS, f16->f32,
 //                   TMEM), then O_t += P_t V_j with P read from TMEM (TS)
-//   warps 0..4*NQT-1  softmax, one warpgroup per Q tile, one thread per row
-//                   (= TMEM lane): tcgen05.ld S, scale/mask in the log2
-//                   domain, running max with lazy rescaling (only when the
-//                   max grows by more than 2^8), P = exp2(S - m) packed to
-//                   half into the S columns, O rescaled in TMEM when needed.
+//
+// With NQT = 2 the two softmax warpgroups ping-pong: while one computes its
+// softmax the tensor core runs the other tile's PV and next S.  The producer
+// warpgroup gives registers to the softmax warpgroups (setmaxnreg).
 //
 // TMEM columns: S_t at t*128 (P_t aliases its first 64), O_t after the S
 // block.  Causal / windowed key tiles outside every row's range are never
@@ -36,8 +41,12 @@ struct PrefillArgs {
     int n_q, n_kv, Hq, Hkv, G, B;
     int tok_per_tile, n_tiles_q, n_cta_q;
     int kv_bdiv;
-    float qk_scale_log2;      // scale * log2(e)            (no softcap)
-    float qk_scale, softcap;  // softcap path: softcap * tanh(raw * scale / softcap)
+    // Pre-exponent value x and multiplier cx, P = 2^(x*cx - m):
+    //   fused (softcap == 0, scale > 0): x = s + (slope/scale)*mask, cx = scale*log2(e)
+    //   otherwise: x = logit (softcap*tanh(s*qk_scale) or s*scale) + slope*mask, cx = log2(e)
+    int fused;
+    float cx;
+    float qk_scale, softcap, scale;
     float max_bias, m0, m1; int n_head_log2;
     int causal, window;
     int q_quant8;             // K was Q8_0: quantize Q rows like ggml's from_float
@@ -53,17 +62,87 @@ template <int D, int NQT> struct PrefillCfg {
     static constexpr int K_OFF = Q_OFF + NQT * TILE_BYTES;
     static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
     static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
-    static constexpr int NBARS = 1 + 3 * STAGES + 2 * NQT + 1;
+    static constexpr int NBARS = 1 + 2 * STAGES + 2 * NQT + 1;
     static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;   // +1024 alignment slack
-    static constexpr int NTHREADS = 128 * NQT + 64;
+    static constexpr int NTHREADS = 128 * NQT + 128;
+    static constexpr int TMA_WARP = 4 * NQT, MMA_WARP = 4 * NQT + 1;
     static constexpr int TMEM_USED = NQT * (128 + D);
     static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
     static constexpr int S_COL = 0;
     static constexpr int O_COL = NQT * 128;
+    // register split (NQT = 2: 384 threads launched at 168 registers)
+    static constexpr int REG_SOFTMAX = 224, REG_PRODUCER = 56;
+    // out of every 8 column pairs, POLY_PAIRS use the FMA-pipe exp2
+#ifdef VTX_POLY_PAIRS
+    static constexpr int POLY_PAIRS = VTX_POLY_PAIRS;
+#else
+    static constexpr int POLY_PAIRS = D == 64 ? 3 : 2;
+#endif
 };
 
 // error codes written to PrefillArgs::err
-enum { VTX_KERR_Q = 1, VTX_KERR_KV = 2, VTX_KERR_S = 3, VTX_KERR_P = 4, VTX_KERR_O = 5, VTX_KERR_EMPTY = 6 };
+enum { VTX_KERR_Q = 1, VTX_KERR_KV = 2, VTX_KERR_S = 3, VTX_KERR_P = 4, VTX_KERR_O = 5 };
+
+// ---- packed f32x2 arithmetic (sm_100) ---------------------------------------
+__device__ __forceinline__ uint64_t pk2(float a, float b) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void upk2(uint64_t r, float &a, float &b) {
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
+
+// 2^x on the FMA pipe for a pair (x <= ~8 here).  Cody-Waite style range
+// reduction x = j + f, j = round(x), |f| <= 1/2, via the 1.5*2^23 rounding
+// constant; 2^f by a degree-3 polynomial fitted here for minimum relative
+// error on [-1/2, 1/2] (max rel. error 7.5e-5, below half an f16 ulp, the
+// precision P is stored in); 2^j added to the exponent field.  x is clamped at
+// -125 so the exponent never leaves the normal range (2^-125 rounds to 0 in
+// the f16 P anyway).
+__device__ __forceinline__ void exp2_poly2(float &a, float &b) {
+    const float kRound = 12582912.0f;                    // 1.5 * 2^23
+    a = fmaxf(a, -125.0f);
+    b = fmaxf(b, -125.0f);
+    const uint64_t x = pk2(a, b);
+    const uint64_t t = fadd2(x, pk2(kRound, kRound));
+    const uint64_t j = fadd2(t, pk2(-kRound, -kRound));
+    const uint64_t f = fadd2(x, j ^ 0x8000000080000000ull);   // x - j
+    uint64_t p = ffma2(pk2(0.055171773f, 0.055171773f), f, pk2(0.24261115f, 0.24261115f));
+    p = ffma2(p, f, pk2(0.69326097f, 0.69326097f));
+    p = ffma2(p, f, pk2(0.99992806f, 0.99992806f));
+    float pa, pb, ta, tb;
+    upk2(p, pa, pb);
+    upk2(t, ta, tb);
+    a = __int_as_float(__float_as_int(pa) + (__float_as_int(ta) << 23));
+    b = __int_as_float(__float_as_int(pb) + (__float_as_int(tb) << 23));
+}
+
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float r;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+    return r;
+}
+__device__ __forceinline__ uint64_t desc64(uint32_t lo, uint32_t hi) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "r"(lo), "r"(hi));
+    return r;
+}
+
+template <int N>
+__device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N)); }
+template <int N>
+__device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
 template <int D, int NQT, bool HAS_MASK>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
@@ -75,9 +154,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *q_full = bars;
-    uint64_t *k_full = bars + 1;
-    uint64_t *v_full = k_full + C::STAGES;
-    uint64_t *kv_empty = v_full + C::STAGES;
+    uint64_t *kv_full = bars + 1;                  // K_j and V_j of a stage landed
+    uint64_t *kv_empty = kv_full + C::STAGES;
     uint64_t *s_full = kv_empty + C::STAGES;
     uint64_t *p_full = s_full + NQT;
     uint64_t *o_full = p_full + NQT;
@@ -104,8 +182,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     if (tid == 0) {
         mbar_init(q_full, 128 * NQT);
         for (int s = 0; s < C::STAGES; ++s) {
-            mbar_init(&k_full[s], 1);
-            mbar_init(&v_full[s], 1);
+            mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
         for (int t = 0; t < NQT; ++t) {
@@ -115,11 +192,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         mbar_init(o_full, 1);
         fence_mbar_init();
     }
-    if (warp == 4 * NQT + 1) {             // MMA warp owns the TMEM allocation
+    if (warp == C::MMA_WARP) {             // MMA warp owns the TMEM allocation
         tmem_alloc(tmem_slot, C::TMEM_COLS);
         tmem_relinquish();
     }
-    if (warp == 4 * NQT && lane == 0) {
+    if (warp == C::TMA_WARP && lane == 0) {
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
     }
@@ -127,10 +204,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    bool ok = true;
 
     if (warp < 4 * NQT) {
+        if (NQT == 2) setmaxnreg_inc<C::REG_SOFTMAX>();
         // =================== softmax warpgroups ===============================
+        bool ok = true;
         const int t = warp >> 2;                   // Q tile within the CTA
         const int r = tid & 127;                   // row == TMEM lane
         const int qt = qt0 + t;
@@ -200,6 +278,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         if (a.max_bias > 0.0f)
             slope = head < a.n_head_log2 ? powf(a.m0, (float)(head + 1))
                                          : powf(a.m1, (float)(2 * (head - a.n_head_log2) + 1));
+        const float mask_mul = a.fused ? slope / a.scale : slope;
         const char *mrow = nullptr;
         if (HAS_MASK && row_ok)
             mrow = a.mask + (long long)tok * a.m_nb1 + (long long)(head % a.m_ne2) * a.m_nb2 +
@@ -208,6 +287,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
         const uint32_t s_addr = tmem + lane_base + C::S_COL + t * 128;
         const uint32_t o_addr = tmem + lane_base + C::O_COL + t * D;
+        const float cx = a.cx;
         float m_run = -INFINITY, l_run = 0.0f;
 
         for (int it = 0; it < n_iter && ok; ++it) {
@@ -226,30 +306,36 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(raw[i]);
             }
             const int k0 = j * C::BN;
-            const bool full = !HAS_MASK && k0 >= lo && k0 + C::BN - 1 <= hi;
-            if (a.softcap != 0.0f) {
+            if (!a.fused) {
 #pragma unroll
-                for (int i = 0; i < 128; ++i) s[i] = a.softcap * tanhf(s[i] * a.qk_scale) * kLog2e;
-            } else {
-#pragma unroll
-                for (int i = 0; i < 128; ++i) s[i] *= a.qk_scale_log2;
+                for (int i = 0; i < 128; ++i)
+                    s[i] = a.softcap != 0.0f ? a.softcap * tanhf(s[i] * a.qk_scale) : s[i] * a.scale;
             }
-            if (!full) {
+            // Padding rows (row_ok false) never need masking: their output is
+            // dropped.  The masking pass runs warp-uniformly so rows that are
+            // fully inside their key range never split the warp.
+            const bool full = !HAS_MASK && (!row_ok || (k0 >= lo && k0 + C::BN - 1 <= hi));
+            if (__any_sync(0xffffffffu, !full)) {
 #pragma unroll
                 for (int i = 0; i < 128; ++i) {
                     const int key = k0 + i;
                     float x = s[i];
-                    if (key < lo || key > hi) x = -INFINITY;
-                    else if (HAS_MASK) {
-                        const float mv = slope * __half2float(reinterpret_cast<const __half *>(mrow)[key]);
-                        x = mv == -INFINITY ? -INFINITY : x + mv * kLog2e;
-                    }
-                    s[i] = x;
+                    if (HAS_MASK && key >= lo && key <= hi)
+                        x = fmaf(mask_mul, __half2float(reinterpret_cast<const __half *>(mrow)[key]), x);
+                    s[i] = (key < lo || key > hi) ? -INFINITY : x;
                 }
             }
-            float mx = s[0];
+            // row max (tree over 8 independent chains)
+            // row max: 8 independent chains of 3-input max
+            float mx8[8];
 #pragma unroll
-            for (int i = 1; i < 128; ++i) mx = fmaxf(mx, s[i]);
+            for (int k = 0; k < 8; ++k) {
+                mx8[k] = fmaxf(s[16 * k], s[16 * k + 1]);
+#pragma unroll
+                for (int i = 2; i < 16; i += 2) mx8[k] = fmax3(mx8[k], s[16 * k + i], s[16 * k + i + 1]);
+            }
+            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                                   fmaxf(mx8[6], mx8[7])) * cx;
             bool rescale = false;
             float alpha = 1.0f;
             if (mx > m_run + 8.0f) {                 // lazy rescale: only on a 2^8 jump
@@ -260,14 +346,30 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 m_run = mx;
                 l_run *= alpha;
             }
-            const float m_use = m_run == -INFINITY ? 0.0f : m_run;
-            float sum = 0.0f;
+            const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
+            // P = 2^(x*cx - m): MUFU for most pairs, FMA-pipe polynomial for the rest
+            uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+            const uint64_t cx2 = pk2(cx, cx), nm2 = pk2(neg_m, neg_m);
 #pragma unroll
-            for (int i = 0; i < 128; ++i) {
-                s[i] = ex2(s[i] - m_use);
-                sum += s[i];
+            for (int pi = 0; pi < 64; ++pi) {
+                float e0, e1;
+                upk2(ffma2(pk2(s[2 * pi], s[2 * pi + 1]), cx2, nm2), e0, e1);
+                if ((pi & 7) >= 8 - C::POLY_PAIRS) {
+                    exp2_poly2(e0, e1);
+                } else {
+                    e0 = ex2(e0);
+                    e1 = ex2(e1);
+                }
+                s[2 * pi] = e0;
+                s[2 * pi + 1] = e1;
+                sum2[pi & 3] = fadd2(sum2[pi & 3], pk2(e0, e1));
             }
-            l_run += sum;
+            {
+                const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
+                float sa, sb;
+                upk2(s01, sa, sb);
+                l_run += sa + sb;
+            }
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t pk[32];
@@ -294,10 +396,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         }
         // ---- epilogue: O / l -> dst ------------------------------------------
         if (ok && n_iter > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, a.err, VTX_KERR_O));
+        // O rows are staged in the (now idle) Q tiles + K/V ring, padded by
+        // 16 B per row, then written back as whole rows with 16 B per lane
+        // (D/4 lanes per row), so every store fills complete 32 B sectors.
+        constexpr int OP = D + 4;                               // staged row pitch (floats)
+        static_assert(NQT * 128 * OP * 4 <= C::BAR_OFF, "O staging overlaps the barriers");
+        float *stage = reinterpret_cast<float *>(smem + C::Q_OFF) + t * 128 * OP;
         if (ok) {
             tc_fence_after();
-            float *out = reinterpret_cast<float *>(a.dst + (long long)tok * a.d_nb2 + (long long)head * a.d_nb1 +
-                                                   (long long)b * a.d_nb3);
             const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
 #pragma unroll
             for (int c = 0; c < D / 32; ++c) {
@@ -309,101 +415,124 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
 #pragma unroll
                     for (int i = 0; i < 32; ++i) o[i] = 0u;
                 }
-                if (row_ok) {
 #pragma unroll
-                    for (int i = 0; i < 32; i += 4) {
-                        float4 v4 = make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                                __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
-                        *reinterpret_cast<float4 *>(out + c * 32 + i) = v4;
-                    }
-                }
+                for (int i = 0; i < 32; i += 4)
+                    *reinterpret_cast<float4 *>(stage + r * OP + c * 32 + i) =
+                        make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
             }
         }
-    } else if (warp == 4 * NQT) {
-        // =================== TMA producer =====================================
-        if (lane == 0) {
-            const int bkv = b / a.kv_bdiv;
-            int issued = 0;
-            for (int it = 0; it < n_iter; ++it) {
-                const int st = it % C::STAGES;
-                if (it >= C::STAGES &&
-                    !mbar_wait(&kv_empty[st], ((it / C::STAGES) - 1) & 1, a.err, VTX_KERR_KV)) break;
-                issued = it + 1;
-                const int y = (j_begin + it) * C::BN;
-                char *ks = smem + C::K_OFF + st * C::TILE_BYTES;
-                char *vs = smem + C::V_OFF + st * C::TILE_BYTES;
-                mbar_arrive_expect_tx(&k_full[st], C::TILE_BYTES);
-#pragma unroll
-                for (int sub = 0; sub < C::SUB; ++sub) tma_load_4d(ks + sub * 16384, &tmK, &k_full[st], sub * 64, y, g, bkv);
-                mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
-#pragma unroll
-                for (int sub = 0; sub < C::SUB; ++sub) tma_load_4d(vs + sub * 16384, &tmV, &v_full[st], sub * 64, y, g, bkv);
-            }
-            // Drain: the last STAGES loads must have landed before this CTA's
-            // shared memory can be released (already true unless a wait failed).
-            for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it) {
-                const int st = it % C::STAGES;
-                mbar_wait(&k_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
-                mbar_wait(&v_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
+        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup's rows are staged
+        if (__all_sync(0xffffffffu, ok)) {
+            constexpr int LPR = D / 4;                         // lanes per row (16 B each)
+            constexpr int RPP = 128 / LPR;                     // rows per pass of the warpgroup
+            const int c4 = r % LPR;
+            for (int rr = r / LPR; rr < rows_per_tile; rr += RPP) {
+                const int tk = qt * a.tok_per_tile + rr / a.G;
+                if (qt >= a.n_tiles_q || tk >= a.n_q) break;
+                const int hd = g * a.G + rr % a.G;
+                float *out = reinterpret_cast<float *>(a.dst + (long long)tk * a.d_nb2 + (long long)hd * a.d_nb1 +
+                                                       (long long)b * a.d_nb3);
+                *reinterpret_cast<float4 *>(out + c4 * 4) = *reinterpret_cast<const float4 *>(stage + rr * OP + c4 * 4);
             }
         }
     } else {
-        // =================== MMA issuer =======================================
-        if (lane == 0 && n_iter > 0) {
-            constexpr uint32_t IDESC_QK = idesc_f16_f32(128, 128, 0, 0);
-            constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, 0, 1);
-            const uint32_t sbase = smem_u32(smem);
-            bool good = mbar_wait(q_full, 0, a.err, VTX_KERR_Q);
-            tc_fence_after();
-            for (int it = 0; it <= n_iter && good; ++it) {
-                const int st = it % C::STAGES;
-                const int pst = (it + C::STAGES - 1) % C::STAGES;
-                if (it < n_iter) {
-                    if (!mbar_wait(&k_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV)) { good = false; break; }
-                }
-                if (it > 0) {
-                    if (!mbar_wait(&v_full[pst], ((it - 1) / C::STAGES) & 1, a.err, VTX_KERR_KV)) { good = false; break; }
-                }
-                tc_fence_after();
-                for (int t = 0; t < NQT; ++t) {
-                    const uint32_t s_tm = tmem + C::S_COL + t * 128;
-                    if (it > 0) {
-                        if (!mbar_wait(&p_full[t], (it - 1) & 1, a.err, VTX_KERR_P)) { good = false; break; }
-                        tc_fence_after();
-                        const uint32_t o_tm = tmem + C::O_COL + t * D;
-                        const uint32_t vbase = sbase + C::V_OFF + pst * C::TILE_BYTES;
+        if (NQT == 2) setmaxnreg_dec<C::REG_PRODUCER>();
+        if (warp == C::TMA_WARP) {
+            // =================== TMA producer =================================
+            if (lane == 0) {
+                const int bkv = b / a.kv_bdiv;
+                int issued = 0;
+                for (int it = 0; it < n_iter; ++it) {
+                    const int st = it % C::STAGES;
+                    if (it >= C::STAGES &&
+                        !mbar_wait(&kv_empty[st], ((it / C::STAGES) - 1) & 1, a.err, VTX_KERR_KV)) break;
+                    issued = it + 1;
+                    const int y = (j_begin + it) * C::BN;
+                    char *ks = smem + C::K_OFF + st * C::TILE_BYTES;
+                    char *vs = smem + C::V_OFF + st * C::TILE_BYTES;
+                    mbar_arrive_expect_tx(&kv_full[st], 2 * C::TILE_BYTES);
 #pragma unroll
-                        for (int kk = 0; kk < 8; ++kk) {
-                            const uint64_t bdesc = smem_desc_sw128(vbase + kk * 2048, 16384, 1024);
-                            mma_f16_ts(o_tm, s_tm + kk * 8, bdesc, IDESC_PV, (it > 1 || kk > 0) ? 1u : 0u);
-                        }
-                    }
-                    if (it < n_iter) {
-                        const uint32_t qbase = sbase + C::Q_OFF + t * C::TILE_BYTES;
-                        const uint32_t kbase = sbase + C::K_OFF + st * C::TILE_BYTES;
+                    for (int sub = 0; sub < C::SUB; ++sub)
+                        tma_load_4d(ks + sub * 16384, &tmK, &kv_full[st], sub * 64, y, g, bkv);
 #pragma unroll
-                        for (int kk = 0; kk < D / 16; ++kk) {
-                            const uint32_t koff = (kk >> 2) * 16384 + (kk & 3) * 32;
-                            const uint64_t adesc = smem_desc_sw128(qbase + koff, 16, 1024);
-                            const uint64_t bdesc = smem_desc_sw128(kbase + koff, 16, 1024);
-                            mma_f16_ss(s_tm, adesc, bdesc, IDESC_QK, kk > 0 ? 1u : 0u);
-                        }
-                        mma_commit(&s_full[t]);
-                    }
+                    for (int sub = 0; sub < C::SUB; ++sub)
+                        tma_load_4d(vs + sub * 16384, &tmV, &kv_full[st], sub * 64, y, g, bkv);
                 }
-                if (!good) break;
-                if (it > 0) mma_commit(&kv_empty[pst]);
+                // Drain: the last STAGES loads must have landed before this CTA's
+                // shared memory is released (already true unless a wait failed).
+                for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it) {
+                    const int st = it % C::STAGES;
+                    mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
+                }
             }
-            mma_commit(o_full);
-            // every MMA of this CTA must be retired before TMEM is released
-            mbar_wait(o_full, 0, a.err, VTX_KERR_O);
+        } else if (warp == C::MMA_WARP) {
+            // =================== MMA issuer ===================================
+            // Descriptor words are built once; per MMA only the low word (start
+            // address >> 4) moves by a compile-time offset, so the issuing
+            // thread spends a few cycles per tcgen05.mma instead of rebuilding
+            // 64-bit descriptors.
+            if (n_iter > 0) {
+                const uint32_t lead = elect_one();     // the warp stays converged
+                constexpr uint32_t IDESC_QK = idesc_f16_f32(128, 128, 0, 0);
+                constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, 0, 1);
+                constexpr uint32_t HI = (1024u >> 4) | (1u << 14) | (2u << 29);   // SBO 1024, v1, SW128
+                const uint32_t sbase = smem_u32(smem);
+                const uint32_t lo_q = ((sbase + C::Q_OFF) >> 4) | (1u << 16);          // LBO 16 B (K-major)
+                const uint32_t lo_k = ((sbase + C::K_OFF) >> 4) | (1u << 16);
+                const uint32_t lo_v = ((sbase + C::V_OFF) >> 4) | ((16384u >> 4) << 16); // LBO: next 64 cols
+                constexpr uint32_t T16 = C::TILE_BYTES >> 4;
+                bool good = __all_sync(0xffffffffu, mbar_wait(q_full, 0, a.err, VTX_KERR_Q));
+                tc_fence_after();
+                for (int it = 0; it <= n_iter && good; ++it) {
+                    const int st = it % C::STAGES;
+                    const int pst = (it + C::STAGES - 1) % C::STAGES;
+                    if (it < n_iter &&
+                        !__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV)))
+                        break;
+                    tc_fence_after();
+                    const uint32_t k_lo = lo_k + st * T16;
+                    const uint32_t v_lo = lo_v + pst * T16;
+#pragma unroll
+                    for (int t = 0; t < NQT; ++t) {
+                        const uint32_t s_tm = tmem + C::S_COL + t * 128;
+                        if (it > 0) {
+                            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], (it - 1) & 1, a.err, VTX_KERR_P))) {
+                                good = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            const uint32_t o_tm = tmem + C::O_COL + t * D;
+                            mma_f16_ts_w(lead, o_tm, s_tm, desc64(v_lo, HI), IDESC_PV, it > 1 ? 1u : 0u);
+#pragma unroll
+                            for (int kk = 1; kk < 8; ++kk)
+                                mma_f16_ts_w(lead, o_tm, s_tm + kk * 8, desc64(v_lo + kk * (2048 >> 4), HI), IDESC_PV, 1u);
+                        }
+                        if (it < n_iter) {
+                            const uint32_t q_lo = lo_q + t * T16;
+                            mma_f16_ss_w(lead, s_tm, desc64(q_lo, HI), desc64(k_lo, HI), IDESC_QK, 0u);
+#pragma unroll
+                            for (int kk = 1; kk < D / 16; ++kk) {
+                                const uint32_t ko = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                                mma_f16_ss_w(lead, s_tm, desc64(q_lo + ko, HI), desc64(k_lo + ko, HI), IDESC_QK, 1u);
+                            }
+                            mma_commit_w(lead, &s_full[t]);
+                        }
+                    }
+                    if (!good) break;
+                    if (it > 0) mma_commit_w(lead, &kv_empty[pst]);
+                }
+                mma_commit_w(lead, o_full);
+                // every MMA of this CTA must be retired before TMEM is released
+                mbar_wait(o_full, 0, a.err, VTX_KERR_O);
+            }
         }
     }
 
     // ---- teardown -------------------------------------------------------------
     tc_fence_before();
     __syncthreads();
-    if (warp == 4 * NQT + 1) {
+    if (warp == C::MMA_WARP) {
         tc_fence_after();
         tmem_dealloc(tmem, C::TMEM_COLS);
     }

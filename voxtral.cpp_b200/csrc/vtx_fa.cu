@@ -440,8 +440,9 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         a.n_q = g.n_q; a.n_kv = g.n_kv; a.Hq = g.Hq; a.Hkv = g.Hkv; a.G = g.G; a.B = g.B;
         a.tok_per_tile = pp.tok_per_tile; a.n_tiles_q = pp.n_tiles_q; a.n_cta_q = pp.n_cta_q;
         a.kv_bdiv = g.B / g.Bkv;
-        a.qk_scale_log2 = params->scale * kLog2e;
-        a.qk_scale = qk_scale; a.softcap = softcap;
+        a.fused = (softcap == 0.0f && params->scale > 0.0f) ? 1 : 0;
+        a.cx = a.fused ? params->scale * kLog2e : kLog2e;
+        a.qk_scale = qk_scale; a.softcap = softcap; a.scale = params->scale;
         a.max_bias = params->max_bias; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
         a.causal = params->causal; a.window = params->window;
         a.q_quant8 = g.kv_type == VTX_TYPE_Q8_0;
