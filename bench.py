@@ -318,7 +318,7 @@ def run_decode(args, rank, world, local):
     import vtx_attn
 
     dev = torch.device("cuda", local)
-    S, Hq, Hkv, D = DEC["n_seq"], DEC["Hq"], DEC["Hkv"], DEC["D"]
+    S, Hq, Hkv, D = args.streams, DEC["Hq"], DEC["Hkv"], DEC["D"]
     rng = np.random.default_rng(4321 + rank)
     lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
     g = torch.Generator(device=dev)
@@ -402,6 +402,7 @@ def main():
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
     ap.add_argument("--workload", default="encoder", choices=["encoder", "decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

@@ -1,0 +1,84 @@
+"""Multi-GPU placement of the attention node: one process per GPU.
+
+voxtral.cpp itself runs one utterance per context on one device (no DP/TP:
+src/voxtral.cpp:2409, :2451 keep static thread_local graph state).  On an
+8 x B200 box the node scales two ways:
+
+* Independent streams / clips per GPU (no collective on the data path).
+  ``lpt_shard`` assigns ragged decode streams to ranks by longest-processing-
+  time bin packing on kv_len, so every rank streams about the same number of
+  KV bytes per decode step; encoder clips are simply dealt round robin.
+* Long-context prefill split by KV head (``head_split_prefill``): rank r owns
+  KV heads [r*Hkv/N, (r+1)*Hkv/N) and the Hq/Hkv query heads of each, runs the
+  attention node on its slice, and one all-gather assembles ggml's
+  [Dv, Hq, n_q, B] result.  All remote bytes move through the collective into
+  local memory; no kernel reads a peer's memory.
+
+The attention callable is injected (default: vtx_attn.flash_attn_ext) so the
+placement logic can be exercised on CPU ranks with any reference function.
+"""
+from __future__ import annotations
+
+from typing import Callable, List, Optional, Sequence
+
+import torch
+
+
+def lpt_shard(kv_len: Sequence[int], n_ranks: int) -> List[List[int]]:
+    """Longest-processing-time bin packing of streams onto ranks by kv_len.
+    Deterministic: ties broken by stream index, then by rank index.  Every
+    stream appears exactly once; each rank's list is in ascending stream id."""
+    if n_ranks <= 0:
+        raise ValueError("n_ranks must be positive")
+    order = sorted(range(len(kv_len)), key=lambda i: (-int(kv_len[i]), i))
+    load = [0] * n_ranks
+    bins: List[List[int]] = [[] for _ in range(n_ranks)]
+    for i in order:
+        r = min(range(n_ranks), key=lambda j: (load[j], j))
+        bins[r].append(i)
+        load[r] += int(kv_len[i])
+    return [sorted(b) for b in bins]
+
+
+def shard_loads(kv_len: Sequence[int], bins: List[List[int]]) -> List[int]:
+    return [sum(int(kv_len[i]) for i in b) for b in bins]
+
+
+def head_range(n_head_kv: int, rank: int, world: int) -> range:
+    if n_head_kv % world:
+        raise ValueError(f"{n_head_kv} KV heads do not split over {world} ranks")
+    per = n_head_kv // world
+    return range(rank * per, (rank + 1) * per)
+
+
+def head_split_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: Optional[torch.Tensor],
+                       scale: float, *, group=None, attn: Optional[Callable] = None, **kw) -> torch.Tensor:
+    """Attention over KV heads split across the ranks of ``group``.
+
+    q: (B, Hq, n_q, D), k/v: (B, Hkv, n_kv, D) — the full views; each rank
+    slices out its heads (views, no copy).  Returns the full (B, n_q, Hq, Dv)
+    result on every rank (ggml's permuted dst), assembled with one
+    all_gather_into_tensor of the per-rank (B, n_q, Hq/N, Dv) slices."""
+    import torch.distributed as dist
+    if attn is None:
+        import vtx_attn
+        attn = vtx_attn.flash_attn_ext
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    B, Hq, n_q = q.shape[0], q.shape[1], q.shape[2]
+    Hkv = k.shape[1]
+    G = Hq // Hkv
+    hr = head_range(Hkv, rank, world)
+    qs = q[:, hr.start * G:hr.stop * G]
+    ks, vs = k[:, hr.start:hr.stop], v[:, hr.start:hr.stop]
+    ms = mask
+    if mask is not None and mask.dim() == 4 and mask.shape[1] == Hq:
+        ms = mask[:, hr.start * G:hr.stop * G]
+    part = attn(qs, ks, vs, ms, scale, **kw)                     # (B, n_q, Hq/N, Dv)
+    part = part.contiguous()
+    Dv = part.shape[-1]
+    # output concatenated along dim 0 (the layout every backend accepts)
+    gathered = torch.empty((world * B,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
+    dist.all_gather_into_tensor(gathered, part, group=group)
+    # (N*B, n_q, Hq/N, Dv) -> (N, B, n_q, Hq/N, Dv) -> (B, n_q, N, Hq/N, Dv) -> (B, n_q, Hq, Dv)
+    return gathered.view((world,) + tuple(part.shape)).permute(1, 2, 0, 3, 4).reshape(B, n_q, Hq, Dv)
