@@ -75,7 +75,9 @@ enum vtx_status {
     VTX_ERR_UNSUPPORTED     = -5,  /* head_dim / parameter not supported    */
     VTX_ERR_WORKSPACE       = -6,  /* workspace too small or misaligned     */
     VTX_ERR_CUDA            = -7,  /* a CUDA launch/runtime call failed     */
-    VTX_ERR_NO_DEVICE       = -8   /* no sm_100 device is current           */
+    VTX_ERR_NO_DEVICE       = -8,  /* no sm_100 device is current           */
+    VTX_ERR_SCRATCH_LIMIT   = -9   /* problem needs more than the built-in
+                                      no-alloc scratch buffer holds         */
 };
 
 /* Mirrors the geometry of a ggml_tensor (ggml.h struct ggml_tensor:
@@ -152,6 +154,30 @@ VTX_API int vtx_flash_attn_decode_batched(const vtx_decode_batch *batch, void *w
                                   size_t workspace_bytes, void *stream);
 
 VTX_API size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *batch);
+
+/* Batched ragged decode for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference (ggml takes scratch from its backend pool).
+ * Some callers have no way to obtain scratch: a plugin running inside a host
+ * application that owns all device memory, code running under a strict
+ * memory budget or a custom allocator that forbids extra cudaMalloc calls,
+ * or a real-time decode loop where an allocation could block.  This entry
+ * point computes exactly what vtx_flash_attn_decode_batched computes but
+ * keeps its split-KV partials in a buffer compiled into the library
+ * (VTX_NOALLOC_SCRATCH_BYTES per GPU, held by every GPU that loads the
+ * library until the process exits).  The caller still passes inputs and
+ * outputs; nothing is allocated.
+ *
+ * - Problems whose partials exceed VTX_NOALLOC_SCRATCH_BYTES are rejected
+ *   with VTX_ERR_SCRATCH_LIMIT (vtx_flash_attn_decode_batched_workspace tells
+ *   how many bytes a batch needs).
+ * - The first call on a device looks up the buffer's device address once
+ *   (cudaGetSymbolAddress); make that first call before any stream capture.
+ * - Every call on a device shares the one buffer: calls that overlap on the
+ *   GPU (different streams, or concurrent host threads) race on it.  Order
+ *   them on one stream or synchronise between them. */
+#define VTX_NOALLOC_SCRATCH_BYTES (32u << 20)
+VTX_API int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *batch, void *stream);
 
 /* Diagnostic: synchronises `stream`, returns and clears the device-side error
  * word of the current device (0 = none).  Kernels set it instead of hanging

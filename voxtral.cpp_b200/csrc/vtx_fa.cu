@@ -361,6 +361,7 @@ const char *vtx_strerror(int status) {
         case VTX_ERR_WORKSPACE: return "workspace too small or misaligned";
         case VTX_ERR_CUDA: return "CUDA launch or runtime call failed";
         case VTX_ERR_NO_DEVICE: return "no sm_100 device is current";
+        case VTX_ERR_SCRATCH_LIMIT: return "problem needs more scratch than the built-in no-alloc buffer holds";
         default: return "unknown status";
     }
 }
@@ -572,3 +573,93 @@ int vtx_read_device_error(void *stream) {
 }
 
 }  // extern "C"
+
+// ================================================================================
+// No-alloc batched decode.
+//
+// For callers that cannot allocate device memory at all (a plugin inside a
+// host application that owns every device allocation, a process under a hard
+// memory budget or a custom allocator, a real-time loop that must not block
+// in cudaMalloc).  The split-KV partials live in this file-scope buffer
+// instead of a caller workspace.  Its host-side name is only a stand-in for
+// the device object, so the device address is looked up once per device with
+// cudaGetSymbolAddress while that device is current, and that pointer is what
+// the kernels receive.  The buffer needs no clearing between calls: every
+// partial the combine kernel reads is written earlier in the same call.
+// Calls on one device share the buffer, so calls that overlap on the GPU race.
+// ================================================================================
+static __device__ __align__(256) unsigned char g_vtx_noalloc_scratch[VTX_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+void *g_noalloc_ptr[kMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+
+int noalloc_scratch(void **out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VTX_ERR_NO_DEVICE;
+    if (!g_noalloc_ptr[dev]) {
+        std::lock_guard<std::mutex> lk(g_noalloc_mu);
+        if (!g_noalloc_ptr[dev]) {
+            void *p = nullptr;
+            if (cudaGetSymbolAddress(&p, g_vtx_noalloc_scratch) != cudaSuccess || !p) {
+                cudaGetLastError();
+                return VTX_ERR_CUDA;
+            }
+            g_noalloc_ptr[dev] = p;
+        }
+    }
+    *out = g_noalloc_ptr[dev];
+    return VTX_OK;
+}
+}  // namespace
+
+extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, void *stream) {
+    if (!b) return VTX_ERR_NULL;
+    if (b->n_seq < 0 || b->n_head_q <= 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv || b->max_kv_len < 0)
+        return VTX_ERR_SHAPE;
+    if (b->head_dim != 64 && b->head_dim != 128) return VTX_ERR_UNSUPPORTED;
+    if (b->kv_type != VTX_TYPE_F16 && b->kv_type != VTX_TYPE_F32 && b->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    if (b->n_seq == 0) return VTX_OK;
+    if (!b->q || !b->k_ptrs || !b->v_ptrs || !b->kv_len || !b->dst) return VTX_ERR_NULL;
+    if (b->n_seq > 65535 || b->n_head_q / b->n_head_kv > 16) return VTX_ERR_UNSUPPORTED;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    const int D = b->head_dim;
+    Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
+          b->n_seq, b->kv_type};
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true);
+    if (sp.part_bytes > (size_t)VTX_NOALLOC_SCRATCH_BYTES) return VTX_ERR_SCRATCH_LIMIT;
+    void *scratch = nullptr;
+    rc = noalloc_scratch(&scratch);
+    if (rc != VTX_OK) return rc;
+    SplitArgs a{};
+    a.q = reinterpret_cast<const char *>(b->q);
+    a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
+    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len;
+    a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
+    a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
+    a.k_bdiv = a.v_bdiv = 1;
+    a.n_kv = g.n_kv;
+    a.dst = reinterpret_cast<char *>(b->dst);
+    a.d_nb1 = (long long)D * 4; a.d_nb2 = (long long)b->n_head_q * D * 4; a.d_nb3 = (long long)b->n_head_q * D * 4;
+    a.n_q = 1; a.Hq = b->n_head_q; a.Hkv = b->n_head_kv; a.G = g.G; a.B = b->n_seq;
+    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
+    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
+    float qk_scale, softcap, m0, m1;
+    int nhl2;
+    fill_math(b->scale, 0.0f, 0.0f, b->n_head_q, &qk_scale, &softcap, &m0, &m1, &nhl2);
+    a.qk_scale = qk_scale; a.softcap = 0.0f; a.max_bias = 0.0f; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
+    a.write_final = sp.n_splits <= 1;
+    if (!a.write_final) {
+        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
+        a.part_o = static_cast<float *>(scratch);
+        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(scratch) + align_up(work * D * 4, 256));
+    }
+    const int rb = row_bytes(b->kv_type, D);
+    a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
+    if (!a.vec) return VTX_ERR_STRIDE;
+    a.err = ds->err;
+    dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
+    return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
+}
