@@ -144,7 +144,11 @@ __device__ __forceinline__ void setmaxnreg_inc() { asm volatile("setmaxnreg.inc.
 template <int N>
 __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N)); }
 
-template <int D, int NQT, bool HAS_MASK>
+// HAS_MASK: an explicit F16 mask tensor is applied.  UNFUSED: softcap or a
+// non-positive scale (logits formed before the exponent); a template flag so
+// the common instantiation carries none of that code (the softmax loop is
+// fully unrolled, and its size is what the instruction cache sees).
+template <int D, int NQT, bool HAS_MASK, bool UNFUSED>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const PrefillArgs a)
@@ -180,14 +184,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     const int n_iter = j_end - j_begin;
 
     if (tid == 0) {
-        mbar_init(q_full, 128 * NQT);
+        mbar_init(q_full, 4 * NQT);               // one arrival per softmax warp
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
         for (int t = 0; t < NQT; ++t) {
             mbar_init(&s_full[t], 1);
-            mbar_init(&p_full[t], 128);
+            mbar_init(&p_full[t], 4);
         }
         mbar_init(o_full, 1);
         fence_mbar_init();
@@ -272,13 +276,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 *reinterpret_cast<uint4 *>(qtile + sub * 16384 + r * 128 + ((cc ^ (r & 7)) << 4)) = pk;
             }
             fence_proxy_async_smem();
-            mbar_arrive(q_full);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_full);
         }
         float slope = 1.0f;
         if (a.max_bias > 0.0f)
             slope = head < a.n_head_log2 ? powf(a.m0, (float)(head + 1))
                                          : powf(a.m1, (float)(2 * (head - a.n_head_log2) + 1));
-        const float mask_mul = a.fused ? slope / a.scale : slope;
+        const float mask_mul = UNFUSED ? slope : slope / a.scale;
         const char *mrow = nullptr;
         if (HAS_MASK && row_ok)
             mrow = a.mask + (long long)tok * a.m_nb1 + (long long)(head % a.m_ne2) * a.m_nb2 +
@@ -306,7 +311,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(raw[i]);
             }
             const int k0 = j * C::BN;
-            if (!a.fused) {
+            if (UNFUSED) {
 #pragma unroll
                 for (int i = 0; i < 128; ++i)
                     s[i] = a.softcap != 0.0f ? a.softcap * tanhf(s[i] * a.qk_scale) : s[i] * a.scale;
@@ -392,7 +397,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             }
             tmem_st_wait();
             tc_fence_before();
-            mbar_arrive(&p_full[t]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[t]);   // per-warp arrival
         }
         // ---- epilogue: O / l -> dst ------------------------------------------
         if (ok && n_iter > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, a.err, VTX_KERR_O));
