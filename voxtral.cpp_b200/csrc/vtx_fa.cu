@@ -24,6 +24,7 @@
 #include "vtx_ptx.cuh"
 #include "fa_splitkv.cuh"
 #include "fa_prefill_sm100.cuh"
+#include "fa_decode_mma.cuh"
 
 using namespace vtx;
 
@@ -296,6 +297,39 @@ int launch_split_d(const SplitArgs &a, int maxr, dim3 grid, cudaStream_t st) {
     return maxr == 4 ? launch_split_t<D, KVT, 4>(a, grid, st) : launch_split_t<D, KVT, 16>(a, grid, st);
 }
 
+// Decode on the streaming mma.sync kernel: F16 K/V, n_q = 1, at most 4 query
+// heads per KV head, 16-byte aligned rows; partials merged by the combine.
+template <int D>
+int launch_decode_mma_t(const SplitArgs &a, cudaStream_t st) {
+    using C = DecodeCfg<D>;
+    static int attr_done[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(fa_decode_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev] = 1;
+    }
+    const long long items = (long long)a.B * a.Hkv * a.n_splits;
+    fa_decode_mma_kernel<D><<<(unsigned)((items + C::WARPS - 1) / C::WARPS), 128, C::SMEM, st>>>(a, (int)items);
+    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (!a.write_final) {
+        const long long rows = (long long)a.B * a.Hkv * a.G;
+        fa_combine_kernel<D, 4><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, a.Hkv);
+        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    }
+    return VTX_OK;
+}
+
+int launch_decode_mma(const SplitArgs &a, int D, cudaStream_t st) {
+    return D == 64 ? launch_decode_mma_t<64>(a, st) : launch_decode_mma_t<128>(a, st);
+}
+
+bool decode_mma_ok(int kv_type, int n_q, int G, int vec, int maxr, int n_hchunks) {
+    return kv_type == VTX_TYPE_F16 && n_q == 1 && G <= 4 && vec == 16 && maxr == 4 && n_hchunks == 1;
+}
+
 int launch_split(const SplitArgs &a, int D, int kvt, int maxr, dim3 grid, cudaStream_t st) {
     if (D == 64) {
         if (kvt == VTX_TYPE_F16) return launch_split_d<64, 1>(a, maxr, grid, st);
@@ -506,6 +540,9 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
                           (unsigned long long)(g.Bkv > 1 ? v->nb[3] : 0)});
     if (!a.vec) return VTX_ERR_STRIDE;
     a.err = ds->err;
+    if (decode_mma_ok(g.kv_type, g.n_q, g.G, a.vec, sp.maxr, sp.n_hchunks) && !mask && !params->causal &&
+        params->logit_softcap == 0.0f)
+        return launch_decode_mma(a, g.D, st);
     dim3 grid((unsigned)(sp.n_splits * sp.n_qtiles), (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)g.B);
     return launch_split(a, g.D, g.kv_type, sp.maxr, grid, st);
 }
@@ -568,6 +605,8 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
     // aligned bases whenever the strides allow 16-byte copies
     if (!a.vec) return VTX_ERR_STRIDE;
     a.err = ds->err;
+    if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
+        return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
     dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
     return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
 }
@@ -676,6 +715,8 @@ extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, 
     a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
     if (!a.vec) return VTX_ERR_STRIDE;
     a.err = ds->err;
+    if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
+        return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
     dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
     return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
 }
