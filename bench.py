@@ -287,28 +287,27 @@ def run_encoder_e2e(args, dev, world, rank):
 
 
 # ---- CPU baseline (oracle = CPU restatement of ggml's flash_attn_ext) -----------
-def cpu_baseline_encoder(budget_s: float = 15.0):
+def cpu_baseline_encoder(budget_s: float = 12.0):
+    """The oracle (CPU restatement of ggml's flash_attn_ext, ggml mode) on whole
+    encoder layers of configs[1], all host cores, until ~budget_s of CPU work
+    (at most the 32 layers of one clip)."""
     import numpy as np
     import oracle as O
-    n, H, D = ENC["n"], ENC["H"], ENC["D"]
+    n, H, D, L = ENC["n"], ENC["H"], ENC["D"], ENC["layers"]
     rng = np.random.default_rng(5)
-    q = rng.standard_normal((n, H, D)).astype(np.float16)
-    k = rng.standard_normal((n, H, D)).astype(np.float16)
-    v = rng.standard_normal((n, H, D)).astype(np.float16)
     view = lambda a: a.transpose(1, 0, 2)[None]
     cores = O.n_cores()
-    rows = 64
-    t0 = time.perf_counter()
-    O.flash_attn_ext(view(q[:rows]), view(k), view(v), None, 0.125, threads=cores)
-    dt = time.perf_counter() - t0
-    rows = int(min(n, max(rows, rows * budget_s / max(dt, 1e-3) * 0.5)))
-    t0 = time.perf_counter()
-    O.flash_attn_ext(view(q[:rows]), view(k), view(v), None, 0.125, threads=cores)
-    dt = time.perf_counter() - t0
-    flops = 4.0 * D * H * rows * n
-    return {"value": round(flops / dt / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
-            "sample": f"1 layer: {rows} query rows x {n} keys x {H} heads x {D} (of 1500 x 32 layers), "
-                      f"ggml-mode oracle, {dt:.2f} s"}
+    layers, spent = 0, 0.0
+    while layers < L and spent < budget_s:
+        q, k, v = (rng.standard_normal((n, H, D)).astype(np.float16) for _ in range(3))
+        t0 = time.perf_counter()
+        O.flash_attn_ext(view(q), view(k), view(v), None, D ** -0.5, threads=cores)
+        spent += time.perf_counter() - t0
+        layers += 1
+    flops = 4.0 * D * H * n * n * layers
+    return {"value": round(flops / spent / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
+            "sample": f"{layers} of the 32 encoder layers of one configs[1] clip (1500 x 1500 x 20 heads x 64 each), "
+                      f"ggml-mode oracle on {cores} threads, {spent:.1f} s"}
 
 
 # ---- decode workload ---------------------------------------------------------------
@@ -376,9 +375,9 @@ def run_reference(args):
     O.build()
     vals = []
     for _ in range(max(0, min(args.warmup, 1))):
-        cpu_baseline_encoder(budget_s=2.0)
+        cpu_baseline_encoder(budget_s=1.0)
     for _ in range(max(1, min(args.steps, 3))):
-        vals.append(cpu_baseline_encoder(budget_s=10.0))
+        vals.append(cpu_baseline_encoder(budget_s=8.0))
     v = sorted(x["value"] for x in vals)[len(vals) // 2]
     cb = dict(vals[0])
     cb["value"] = v
@@ -402,6 +401,7 @@ def main():
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
     ap.add_argument("--workload", default="encoder", choices=["encoder", "decode"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
@@ -418,6 +418,14 @@ def main():
     rank, world, local = dist_setup(args.gpus)
     if args.workload == "encoder":
         res = run_encoder(args, rank, world, local)
+        if not args.no_decode:
+            # the decode half of the metric (KV GB/s, configs[4]), timed after
+            # and separately from the encoder steps above
+            import copy
+            dargs = copy.copy(args)
+            dargs.steps, dargs.warmup = 5, 3
+            d = run_decode(dargs, rank, world, local)
+            res["decode"] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "config")}
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
