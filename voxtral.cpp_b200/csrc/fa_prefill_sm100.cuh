@@ -12,20 +12,25 @@
 //                   tcgen05.ld S, max, P = 2^(x*c - m) (MUFU ex2 for most
 //                   columns, a degree-3 polynomial on the FMA pipe for the
 //                   rest), lazy rescaling (only when the row max grows by more
-//                   than 2^8), P packed to half into the S columns of TMEM.
+//                   than 2^8), P packed to half into its TMEM columns.
 //   WG NQT warp 0   TMA producer: K_j, V_j (128 keys x D, 128-byte swizzle)
 //                   into a STAGES-deep shared-memory ring (mbarrier tx count)
 //   WG NQT warp 1   MMA issuer (one thread): S_t = Q_t K_j^T  (SS, f16->f32,
 //                   TMEM), then O_t += P_t V_j with P read from TMEM (TS)
 //
-// With NQT = 2 the two softmax warpgroups ping-pong: while one computes its
+// With NQT = 2 the two softmax warpgroups share the SM: while one computes its
 // softmax the tensor core runs the other tile's PV and next S.  The producer
 // warpgroup gives registers to the softmax warpgroups (setmaxnreg).
 //
-// TMEM columns: S_t at t*128 (P_t aliases its first 64), O_t after the S
-// block.  Causal / windowed key tiles outside every row's range are never
-// loaded.  Numerics: Q and P in f16 (Q is rounded to half exactly as ggml
-// rounds Q for an F16 K), fp32 accumulation of S and O.
+// TMEM columns, look-ahead layout (D = 64, or NQT = 1): per tile S_t (128),
+// P_t (64, f16 pairs), O_t (D).  The softmax releases S_t as soon as it sits
+// in registers, so S_t(j+1) = Q_t K_{j+1}^T runs during the softmax of tile
+// j and the softmax warps never wait for the tensor core in steady state.
+// Otherwise (D = 128, NQT = 2: 640 columns would be needed) P_t aliases the
+// first 64 columns of S_t and O_t sits after the S block.  Causal / windowed
+// key tiles outside every row's range are never loaded.  Numerics: Q and P
+// in f16 (Q is rounded to half exactly as ggml rounds Q for an F16 K), fp32
+// accumulation of S and O.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -62,14 +67,20 @@ template <int D, int NQT> struct PrefillCfg {
     static constexpr int K_OFF = Q_OFF + NQT * TILE_BYTES;
     static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
     static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
-    static constexpr int NBARS = 1 + 2 * STAGES + 2 * NQT + 1;
+    // Look-ahead (LA): when every tile can own S (128 columns), P (64) and O
+    // (D) in TMEM, P gets its own columns and Q K^T of the next key tile runs
+    // while the softmax of the current one is still computing.  Otherwise P
+    // aliases S and the next S waits for P V.
+    static constexpr bool LA = NQT * (128 + 64 + D) <= 512;
+    static constexpr int NBARS = 1 + 2 * STAGES + 4 * NQT + 1;
     static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;   // +1024 alignment slack
     static constexpr int NTHREADS = 128 * NQT + 128;
     static constexpr int TMA_WARP = 4 * NQT, MMA_WARP = 4 * NQT + 1;
-    static constexpr int TMEM_USED = NQT * (128 + D);
+    static constexpr int TMEM_USED = LA ? NQT * (192 + D) : NQT * (128 + D);
     static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
-    static constexpr int S_COL = 0;
-    static constexpr int O_COL = NQT * 128;
+    __host__ __device__ static constexpr int s_col(int t) { return LA ? t * (192 + D) : t * 128; }
+    __host__ __device__ static constexpr int p_col(int t) { return LA ? s_col(t) + 128 : s_col(t); }
+    __host__ __device__ static constexpr int o_col(int t) { return LA ? s_col(t) + 192 : NQT * 128 + t * D; }
     // register split (NQT = 2: 384 threads launched at 168 registers)
     static constexpr int REG_SOFTMAX = 224, REG_PRODUCER = 56;
     // out of every 8 column pairs, POLY_PAIRS use the FMA-pipe exp2
@@ -102,6 +113,11 @@ __device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
     asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
     return d;
 }
+__device__ __forceinline__ uint64_t fsub2(uint64_t a, uint64_t b) {
+    uint64_t d;
+    asm("sub.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+    return d;
+}
 
 // 2^x on the FMA pipe for a pair (x <= ~8 here).  Cody-Waite style range
 // reduction x = j + f, j = round(x), |f| <= 1/2, via the 1.5*2^23 rounding
@@ -117,7 +133,7 @@ __device__ __forceinline__ void exp2_poly2(float &a, float &b) {
     const uint64_t x = pk2(a, b);
     const uint64_t t = fadd2(x, pk2(kRound, kRound));
     const uint64_t j = fadd2(t, pk2(-kRound, -kRound));
-    const uint64_t f = fadd2(x, j ^ 0x8000000080000000ull);   // x - j
+    const uint64_t f = fsub2(x, j);
     uint64_t p = ffma2(pk2(0.055171773f, 0.055171773f), f, pk2(0.24261115f, 0.24261115f));
     p = ffma2(p, f, pk2(0.69326097f, 0.69326097f));
     p = ffma2(p, f, pk2(0.99992806f, 0.99992806f));
@@ -162,7 +178,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     uint64_t *kv_empty = kv_full + C::STAGES;
     uint64_t *s_full = kv_empty + C::STAGES;
     uint64_t *p_full = s_full + NQT;
-    uint64_t *o_full = p_full + NQT;
+    uint64_t *s_free = p_full + NQT;               // LA: S_t copied to registers, may be overwritten
+    uint64_t *pv_done = s_free + NQT;              // LA: O_t += P_t V done, P_t may be rewritten
+    uint64_t *o_full = pv_done + NQT;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -192,6 +210,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         for (int t = 0; t < NQT; ++t) {
             mbar_init(&s_full[t], 1);
             mbar_init(&p_full[t], 4);
+            mbar_init(&s_free[t], 4);
+            mbar_init(&pv_done[t], 1);
         }
         mbar_init(o_full, 1);
         fence_mbar_init();
@@ -290,8 +310,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                    (long long)(b % a.m_ne3) * a.m_nb3;
 
         const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t s_addr = tmem + lane_base + C::S_COL + t * 128;
-        const uint32_t o_addr = tmem + lane_base + C::O_COL + t * D;
+        const uint32_t s_addr = tmem + lane_base + C::s_col(t);
+        const uint32_t p_addr = tmem + lane_base + C::p_col(t);
+        const uint32_t o_addr = tmem + lane_base + C::o_col(t);
         const float cx = a.cx;
         float m_run = -INFINITY, l_run = 0.0f;
 
@@ -309,6 +330,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 tmem_ld_wait();
 #pragma unroll
                 for (int i = 0; i < 128; ++i) s[i] = __uint_as_float(raw[i]);
+            }
+            if constexpr (C::LA) {                   // S_t is in registers: the next Q K^T may overwrite it
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&s_free[t]);
             }
             const int k0 = j * C::BN;
             if (UNFUSED) {
@@ -375,12 +401,17 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 upk2(s01, sa, sb);
                 l_run += sa + sb;
             }
+            if (C::LA && it > 0) {                  // P_t and O_t are free once the previous P V retired
+                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (it - 1) & 1, a.err, VTX_KERR_O));
+                if (!ok) break;
+                tc_fence_after();
+            }
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
                 uint32_t pk[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) pk[i] = pack_half2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
-                tmem_st32(s_addr + c * 32, pk);
+                tmem_st32(p_addr + c * 32, pk);
             }
             // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
             // rescales if any of its rows needs it (alpha == 1 for the others).
@@ -490,40 +521,89 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 constexpr uint32_t T16 = C::TILE_BYTES >> 4;
                 bool good = __all_sync(0xffffffffu, mbar_wait(q_full, 0, a.err, VTX_KERR_Q));
                 tc_fence_after();
-                for (int it = 0; it <= n_iter && good; ++it) {
+                // S_t = Q_t K^T of the key tile in stage `kst`
+                auto issue_qk = [&](int t, int kst) {
+                    const uint32_t s_tm = tmem + C::s_col(t);
+                    const uint32_t q_lo = lo_q + t * T16;
+                    const uint32_t k_lo = lo_k + kst * T16;
+                    mma_f16_ss_w(lead, s_tm, desc64(q_lo, HI), desc64(k_lo, HI), IDESC_QK, 0u);
+#pragma unroll
+                    for (int kk = 1; kk < D / 16; ++kk) {
+                        const uint32_t ko = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
+                        mma_f16_ss_w(lead, s_tm, desc64(q_lo + ko, HI), desc64(k_lo + ko, HI), IDESC_QK, 1u);
+                    }
+                    mma_commit_w(lead, &s_full[t]);
+                };
+                // O_t (+)= P_t V of the key tile in stage `vst`
+                auto issue_pv = [&](int t, int vst, uint32_t acc) {
+                    const uint32_t p_tm = tmem + C::p_col(t);
+                    const uint32_t o_tm = tmem + C::o_col(t);
+                    const uint32_t v_lo = lo_v + vst * T16;
+                    mma_f16_ts_w(lead, o_tm, p_tm, desc64(v_lo, HI), IDESC_PV, acc);
+#pragma unroll
+                    for (int kk = 1; kk < 8; ++kk)
+                        mma_f16_ts_w(lead, o_tm, p_tm + kk * 8, desc64(v_lo + kk * (2048 >> 4), HI), IDESC_PV, 1u);
+                };
+                if constexpr (C::LA) {
+                    // Issue order per key tile it: S(it+1) for every Q tile as soon
+                    // as its softmax has copied S(it) out, then O += P(it) V(it).
+                    if (good) good = __all_sync(0xffffffffu, mbar_wait(&kv_full[0], 0, a.err, VTX_KERR_KV));
+                    tc_fence_after();
+                    if (good) {
+#pragma unroll
+                        for (int t = 0; t < NQT; ++t) issue_qk(t, 0);
+                    }
+                    for (int it = 0; it < n_iter && good; ++it) {
+                        const int st = it % C::STAGES;
+                        if (it + 1 < n_iter) {
+                            const int nst = (it + 1) % C::STAGES;
+                            if (!__all_sync(0xffffffffu, mbar_wait(&kv_full[nst], ((it + 1) / C::STAGES) & 1, a.err, VTX_KERR_KV))) {
+                                good = false;
+                                break;
+                            }
+#pragma unroll
+                            for (int t = 0; t < NQT; ++t) {
+                                if (!__all_sync(0xffffffffu, mbar_wait(&s_free[t], it & 1, a.err, VTX_KERR_S))) {
+                                    good = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                issue_qk(t, nst);
+                            }
+                            if (!good) break;
+                        }
+#pragma unroll
+                        for (int t = 0; t < NQT; ++t) {
+                            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], it & 1, a.err, VTX_KERR_P))) {
+                                good = false;
+                                break;
+                            }
+                            tc_fence_after();
+                            issue_pv(t, st, it > 0 ? 1u : 0u);
+                            mma_commit_w(lead, &pv_done[t]);
+                        }
+                        if (!good) break;
+                        mma_commit_w(lead, &kv_empty[st]);
+                    }
+                }
+                for (int it = 0; !C::LA && it <= n_iter && good; ++it) {
                     const int st = it % C::STAGES;
                     const int pst = (it + C::STAGES - 1) % C::STAGES;
                     if (it < n_iter &&
                         !__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV)))
                         break;
                     tc_fence_after();
-                    const uint32_t k_lo = lo_k + st * T16;
-                    const uint32_t v_lo = lo_v + pst * T16;
 #pragma unroll
                     for (int t = 0; t < NQT; ++t) {
-                        const uint32_t s_tm = tmem + C::S_COL + t * 128;
                         if (it > 0) {
                             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], (it - 1) & 1, a.err, VTX_KERR_P))) {
                                 good = false;
                                 break;
                             }
                             tc_fence_after();
-                            const uint32_t o_tm = tmem + C::O_COL + t * D;
-                            mma_f16_ts_w(lead, o_tm, s_tm, desc64(v_lo, HI), IDESC_PV, it > 1 ? 1u : 0u);
-#pragma unroll
-                            for (int kk = 1; kk < 8; ++kk)
-                                mma_f16_ts_w(lead, o_tm, s_tm + kk * 8, desc64(v_lo + kk * (2048 >> 4), HI), IDESC_PV, 1u);
+                            issue_pv(t, pst, it > 1 ? 1u : 0u);
                         }
-                        if (it < n_iter) {
-                            const uint32_t q_lo = lo_q + t * T16;
-                            mma_f16_ss_w(lead, s_tm, desc64(q_lo, HI), desc64(k_lo, HI), IDESC_QK, 0u);
-#pragma unroll
-                            for (int kk = 1; kk < D / 16; ++kk) {
-                                const uint32_t ko = ((kk >> 2) * 16384 + (kk & 3) * 32) >> 4;
-                                mma_f16_ss_w(lead, s_tm, desc64(q_lo + ko, HI), desc64(k_lo + ko, HI), IDESC_QK, 1u);
-                            }
-                            mma_commit_w(lead, &s_full[t]);
-                        }
+                        if (it < n_iter) issue_qk(t, st);
                     }
                     if (!good) break;
                     if (it > 0) mma_commit_w(lead, &kv_empty[pst]);
