@@ -55,6 +55,7 @@ struct PrefillArgs {
     float max_bias, m0, m1; int n_head_log2;
     int causal, window;
     int q_quant8;             // K was Q8_0: quantize Q rows like ggml's from_float
+    int o_tma;                // dst written by TMA stores through tmO (aligned F32 dst)
     int *err;
 };
 
@@ -167,7 +168,7 @@ __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.
 template <int D, int NQT, bool HAS_MASK, bool UNFUSED>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                        const PrefillArgs a)
+                        const __grid_constant__ CUtensorMap tmO, const PrefillArgs a)
 {
     using C = PrefillCfg<D, NQT>;
     extern __shared__ __align__(1024) char smem_raw[];
@@ -248,50 +249,60 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 if (a.window > 0) lo = max(0, tok + off - (a.window - 1));
             }
         }
-        // Q row -> f16 -> swizzled smem (K-major, 128B swizzle, 64-col sub-tiles)
+        // Q row -> f16 -> swizzled smem (K-major, 128B swizzle, 64-col sub-tiles).
+        // The whole row is loaded into registers before anything is stored: the
+        // shared-memory stores go through a generic pointer, so loads placed
+        // after them could not be hoisted and each would pay a DRAM latency.
         {
             char *qtile = smem + C::Q_OFF + t * C::TILE_BYTES;
             const char *src = a.q + (long long)tok * a.q_nb1 + (long long)head * a.q_nb2 + (long long)b * a.q_nb3;
-            float qabs[D / 32];
+            float f[D];
+            if (row_ok) {
+                if (a.q_f16) {
+                    uint4 raw[D / 8];
 #pragma unroll
-            for (int i = 0; i < D / 32; ++i) qabs[i] = 0.0f;
-            if (a.q_quant8 && row_ok) {
-                for (int d = 0; d < D; ++d) {
-                    const float x = a.q_f16 ? __half2float(reinterpret_cast<const __half *>(src)[d])
-                                            : reinterpret_cast<const float *>(src)[d];
-                    qabs[d >> 5] = fmaxf(qabs[d >> 5], fabsf(x));
-                }
-            }
+                    for (int c = 0; c < D / 8; ++c) raw[c] = *reinterpret_cast<const uint4 *>(src + c * 16);
 #pragma unroll
-            for (int c = 0; c < D / 8; ++c) {
-                uint4 pk = make_uint4(0, 0, 0, 0);
-                if (row_ok) {
-                    float f[8];
-                    if (a.q_f16) {
-                        const uint4 raw = *reinterpret_cast<const uint4 *>(src + c * 16);
-                        const __half2 *h = reinterpret_cast<const __half2 *>(&raw);
+                    for (int c = 0; c < D / 8; ++c) {
+                        const __half2 *h = reinterpret_cast<const __half2 *>(&raw[c]);
 #pragma unroll
-                        for (int i = 0; i < 4; ++i) { float2 x = __half22float2(h[i]); f[2 * i] = x.x; f[2 * i + 1] = x.y; }
-                    } else {
-                        const float4 x0 = *reinterpret_cast<const float4 *>(src + c * 32);
-                        const float4 x1 = *reinterpret_cast<const float4 *>(src + c * 32 + 16);
-                        f[0] = x0.x; f[1] = x0.y; f[2] = x0.z; f[3] = x0.w;
-                        f[4] = x1.x; f[5] = x1.y; f[6] = x1.z; f[7] = x1.w;
+                        for (int i = 0; i < 4; ++i) {
+                            const float2 x = __half22float2(h[i]);
+                            f[8 * c + 2 * i] = x.x;
+                            f[8 * c + 2 * i + 1] = x.y;
+                        }
                     }
-                    if (a.q_quant8) {
-                        // K is Q8_0 in the caller's tensor: ggml quantizes Q to Q8_0
-                        // (per 32 values: d = amax/127, q = rne(x*127/amax)) before
-                        // the dot; reproduce that and feed d*q (as half) to the MMA.
-                        const int blk = c >> 2;
-                        const float amax = qabs[blk];
+                } else {
+#pragma unroll
+                    for (int c = 0; c < D / 4; ++c) {
+                        const float4 x = *reinterpret_cast<const float4 *>(src + c * 16);
+                        f[4 * c] = x.x; f[4 * c + 1] = x.y; f[4 * c + 2] = x.z; f[4 * c + 3] = x.w;
+                    }
+                }
+                if (a.q_quant8) {
+                    // K is Q8_0 in the caller's tensor: ggml quantizes Q to Q8_0
+                    // (per 32 values: d = amax/127, q = rne(x*127/amax)) before
+                    // the dot; reproduce that and feed d*q (as half) to the MMA.
+#pragma unroll
+                    for (int blk = 0; blk < D / 32; ++blk) {
+                        float amax = 0.0f;
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(f[32 * blk + i]));
                         const float dq = __half2float(__float2half_rn(amax / 127.0f));
                         const float id = amax != 0.0f ? 127.0f / amax : 0.0f;
 #pragma unroll
-                        for (int i = 0; i < 8; ++i) f[i] = dq * (float)__float2int_rn(f[i] * id);
+                        for (int i = 0; i < 32; ++i) f[32 * blk + i] = dq * (float)__float2int_rn(f[32 * blk + i] * id);
                     }
-                    pk.x = pack_half2(f[0], f[1]); pk.y = pack_half2(f[2], f[3]);
-                    pk.z = pack_half2(f[4], f[5]); pk.w = pack_half2(f[6], f[7]);
                 }
+            } else {
+#pragma unroll
+                for (int i = 0; i < D; ++i) f[i] = 0.0f;
+            }
+#pragma unroll
+            for (int c = 0; c < D / 8; ++c) {
+                uint4 pk;
+                pk.x = pack_half2(f[8 * c], f[8 * c + 1]); pk.y = pack_half2(f[8 * c + 2], f[8 * c + 3]);
+                pk.z = pack_half2(f[8 * c + 4], f[8 * c + 5]); pk.w = pack_half2(f[8 * c + 6], f[8 * c + 7]);
                 const int sub = c >> 3, cc = c & 7;
                 *reinterpret_cast<uint4 *>(qtile + sub * 16384 + r * 128 + ((cc ^ (r & 7)) << 4)) = pk;
             }
@@ -401,18 +412,18 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 upk2(s01, sa, sb);
                 l_run += sa + sb;
             }
+            // P packed to half pairs before any wait, so the conversions can be
+            // scheduled among the exponentials
+            uint32_t pk[64];
+#pragma unroll
+            for (int i = 0; i < 64; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
             if (C::LA && it > 0) {                  // P_t and O_t are free once the previous P V retired
                 ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (it - 1) & 1, a.err, VTX_KERR_O));
                 if (!ok) break;
                 tc_fence_after();
             }
-#pragma unroll
-            for (int c = 0; c < 2; ++c) {
-                uint32_t pk[32];
-#pragma unroll
-                for (int i = 0; i < 32; ++i) pk[i] = pack_half2(s[c * 64 + 2 * i], s[c * 64 + 2 * i + 1]);
-                tmem_st32(p_addr + c * 32, pk);
-            }
+            tmem_st32(p_addr, *reinterpret_cast<const uint32_t(*)[32]>(&pk[0]));
+            tmem_st32(p_addr + 32, *reinterpret_cast<const uint32_t(*)[32]>(&pk[32]));
             // tcgen05.ld/st are warp-collective (.sync.aligned): the whole warp
             // rescales if any of its rows needs it (alpha == 1 for the others).
             if (__any_sync(0xffffffffu, rescale)) {
@@ -433,44 +444,96 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         }
         // ---- epilogue: O / l -> dst ------------------------------------------
         if (ok && n_iter > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, a.err, VTX_KERR_O));
-        // O rows are staged in the (now idle) Q tiles + K/V ring, padded by
-        // 16 B per row, then written back as whole rows with 16 B per lane
-        // (D/4 lanes per row), so every store fills complete 32 B sectors.
-        constexpr int OP = D + 4;                               // staged row pitch (floats)
-        static_assert(NQT * 128 * OP * 4 <= C::BAR_OFF, "O staging overlaps the barriers");
-        float *stage = reinterpret_cast<float *>(smem + C::Q_OFF) + t * 128 * OP;
-        if (ok) {
-            tc_fence_after();
-            const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
+        // After o_full every MMA has retired and every TMA load has landed, so
+        // the Q tiles and the K/V ring are free to stage O.
+        if (a.o_tma) {
+            // Staged as D/32 boxes of [128 rows][32 floats] per tile in the 128-byte
+            // swizzled layout of the output tensor map (conflict-free: a row's
+            // 16-byte chunk c sits at chunk c ^ (row & 7)), then written by one
+            // TMA store per box; rows past the end of the sequence are clipped by
+            // the hardware.
+            static_assert(NQT * (D / 32) * 16384 <= C::BAR_OFF, "O staging overlaps the barriers");
+            char *st = smem + C::Q_OFF + t * (D / 32) * 16384;
+            if (ok) {
+                tc_fence_after();
+                const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
-                uint32_t o[32];
-                if (n_iter > 0) {
-                    tmem_ld32(o_addr + c * 32, o);
-                    tmem_ld_wait();
-                } else {
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    if (n_iter > 0) {
+                        tmem_ld32(o_addr + c * 32, o);
+                        tmem_ld_wait();
+                    } else {
 #pragma unroll
-                    for (int i = 0; i < 32; ++i) o[i] = 0u;
+                        for (int i = 0; i < 32; ++i) o[i] = 0u;
+                    }
+#pragma unroll
+                    for (int q4 = 0; q4 < 8; ++q4)
+                        *reinterpret_cast<float4 *>(st + c * 16384 + r * 128 + ((q4 ^ (r & 7)) << 4)) =
+                            make_float4(__uint_as_float(o[4 * q4]) * inv, __uint_as_float(o[4 * q4 + 1]) * inv,
+                                        __uint_as_float(o[4 * q4 + 2]) * inv, __uint_as_float(o[4 * q4 + 3]) * inv);
                 }
-#pragma unroll
-                for (int i = 0; i < 32; i += 4)
-                    *reinterpret_cast<float4 *>(stage + r * OP + c * 32 + i) =
-                        make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
-                                    __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
             }
-        }
-        asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup's rows are staged
-        if (__all_sync(0xffffffffu, ok)) {
-            constexpr int LPR = D / 4;                         // lanes per row (16 B each)
-            constexpr int RPP = 128 / LPR;                     // rows per pass of the warpgroup
-            const int c4 = r % LPR;
-            for (int rr = r / LPR; rr < rows_per_tile; rr += RPP) {
-                const int tk = qt * a.tok_per_tile + rr / a.G;
-                if (qt >= a.n_tiles_q || tk >= a.n_q) break;
-                const int hd = g * a.G + rr % a.G;
-                float *out = reinterpret_cast<float *>(a.dst + (long long)tk * a.d_nb2 + (long long)hd * a.d_nb1 +
-                                                       (long long)b * a.d_nb3);
-                *reinterpret_cast<float4 *>(out + c4 * 4) = *reinterpret_cast<const float4 *>(stage + rr * OP + c4 * 4);
+            fence_proxy_async_smem();
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this tile's rows are staged
+            if (__all_sync(0xffffffffu, ok) && r == 0 && qt < a.n_tiles_q) {
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c)
+                    tma_store_4d(&tmO, st + c * 16384, c * 32, g * a.G, qt * a.tok_per_tile, b);
+                bulk_commit();
+                bulk_wait_read_all();   // shared memory must stay valid until the stores have read it
+            }
+        } else {
+            // O rows are staged in the (now idle) Q tiles + K/V ring, padded by
+            // 16 B per row, then written back as whole rows with 16 B per lane
+            // (D/4 lanes per row), so every store fills complete 32 B sectors.
+            constexpr int OP = D + 4;                               // staged row pitch (floats)
+            static_assert(NQT * 128 * OP * 4 <= C::BAR_OFF, "O staging overlaps the barriers");
+            float *stage = reinterpret_cast<float *>(smem + C::Q_OFF) + t * 128 * OP;
+            if (ok) {
+                tc_fence_after();
+                const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) {
+                    uint32_t o[32];
+                    if (n_iter > 0) {
+                        tmem_ld32(o_addr + c * 32, o);
+                        tmem_ld_wait();
+                    } else {
+#pragma unroll
+                        for (int i = 0; i < 32; ++i) o[i] = 0u;
+                    }
+#pragma unroll
+                    for (int i = 0; i < 32; i += 4)
+                        *reinterpret_cast<float4 *>(stage + r * OP + c * 32 + i) =
+                            make_float4(__uint_as_float(o[i]) * inv, __uint_as_float(o[i + 1]) * inv,
+                                        __uint_as_float(o[i + 2]) * inv, __uint_as_float(o[i + 3]) * inv);
+                }
+            }
+            asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this warpgroup's rows are staged
+            if (__all_sync(0xffffffffu, ok)) {
+                constexpr int LPR = D / 4;                         // lanes per row (16 B each)
+                constexpr int RPP = 128 / LPR;                     // rows per pass of the warpgroup
+                const int c4 = r % LPR;
+                int rr = r / LPR;
+                if (qt < a.n_tiles_q && rr < rows_per_tile) {
+                    // row rr = token-in-tile * G + head-in-group; advanced by RPP rows per
+                    // pass with one division up front instead of one per row
+                    int tk = qt * a.tok_per_tile + rr / a.G, hl = rr % a.G;
+                    const int tk_step = RPP / a.G, hl_step = RPP % a.G;
+                    const char *base = a.dst + (long long)b * a.d_nb3 + (long long)g * a.G * a.d_nb1 + c4 * 16;
+                    for (; rr < rows_per_tile && tk < a.n_q; rr += RPP) {
+                        *reinterpret_cast<float4 *>(const_cast<char *>(base) + (long long)tk * a.d_nb2 +
+                                                    (long long)hl * a.d_nb1) =
+                            *reinterpret_cast<const float4 *>(stage + rr * OP + c4 * 4);
+                        hl += hl_step;
+                        tk += tk_step;
+                        if (hl >= a.G) {
+                            hl -= a.G;
+                            ++tk;
+                        }
+                    }
+                }
             }
         }
     } else {

@@ -261,6 +261,29 @@ int encode_kv_map(CUtensorMap *m, const void *ptr, int D, int n_kv, int H, int B
     return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
 }
 
+// Output map for the prefill epilogue's TMA stores: F32 [D, Hq, n_q, B] with
+// boxes of 32 columns x G heads x tok_per_tile tokens (one 128-row Q tile).
+// Returns VTX_ERR_STRIDE when the destination cannot be described (base or
+// strides not 16-byte multiples); the caller then uses plain stores.
+int encode_out_map(CUtensorMap *m, void *ptr, int D, int Hq, int n_q, int B, size_t nb1, size_t nb2, size_t nb3,
+                   int G, int tok_per_tile) {
+    if (!g_encode) return VTX_ERR_CUDA;
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 || G > 256 || tok_per_tile > 256) return VTX_ERR_STRIDE;
+    const size_t s1 = Hq > 1 ? nb1 : (size_t)D * 4;          // extent-1 dimensions: any legal stride
+    const size_t s2 = n_q > 1 ? nb2 : s1 * (size_t)Hq;
+    const size_t s3 = B > 1 ? nb3 : s2 * (size_t)n_q;
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hq, (cuuint64_t)n_q, (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)s1, (cuuint64_t)s2, (cuuint64_t)s3};
+    for (int i = 0; i < 3; ++i)
+        if (strides[i] % 16 || strides[i] == 0) return VTX_ERR_STRIDE;
+    cuuint32_t box[4] = {32, (cuuint32_t)G, (cuuint32_t)tok_per_tile, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
+}
+
 void fill_math(float scale, float max_bias, float softcap, int Hq, float *qk_scale, float *softcap_out, float *m0,
                float *m1, int *n_head_log2) {
     *n_head_log2 = 1 << (int)std::floor(std::log2((double)Hq));
@@ -353,8 +376,8 @@ int pick_vec(int row, std::initializer_list<unsigned long long> vals) {
 }
 
 template <int D, int NQT, bool HM, bool UF>
-int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const PrefillArgs &a, dim3 grid,
-                     cudaStream_t st) {
+int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const PrefillArgs &a,
+                     dim3 grid, cudaStream_t st) {
     using C = PrefillCfg<D, NQT>;
     static int attr_done[kMaxDevices] = {0};
     int dev = 0;
@@ -365,27 +388,27 @@ int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const Prefill
             return VTX_ERR_CUDA;
         attr_done[dev] = 1;
     }
-    fa_prefill_sm100_kernel<D, NQT, HM, UF><<<grid, C::NTHREADS, C::SMEM, st>>>(mk, mv, a);
+    fa_prefill_sm100_kernel<D, NQT, HM, UF><<<grid, C::NTHREADS, C::SMEM, st>>>(mk, mv, mo, a);
     return cudaGetLastError() == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
 }
 
 template <int D, int NQT>
-int launch_prefill_d(bool hm, bool uf, const CUtensorMap &mk, const CUtensorMap &mv, const PrefillArgs &a, dim3 grid,
-                     cudaStream_t st) {
-    if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, a, grid, st)
-                      : launch_prefill_t<D, NQT, false, true>(mk, mv, a, grid, st);
-    return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, a, grid, st)
-              : launch_prefill_t<D, NQT, false, false>(mk, mv, a, grid, st);
+int launch_prefill_d(bool hm, bool uf, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
+                     const PrefillArgs &a, dim3 grid, cudaStream_t st) {
+    if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, mo, a, grid, st)
+                      : launch_prefill_t<D, NQT, false, true>(mk, mv, mo, a, grid, st);
+    return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, mo, a, grid, st)
+              : launch_prefill_t<D, NQT, false, false>(mk, mv, mo, a, grid, st);
 }
 
-int launch_prefill(int D, int nqt, bool hm, const CUtensorMap &mk, const CUtensorMap &mv, const PrefillArgs &a,
-                   dim3 grid, cudaStream_t st) {
+int launch_prefill(int D, int nqt, bool hm, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
+                   const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     const bool uf = !a.fused;
     if (D == 64)
-        return nqt == 2 ? launch_prefill_d<64, 2>(hm, uf, mk, mv, a, grid, st)
-                        : launch_prefill_d<64, 1>(hm, uf, mk, mv, a, grid, st);
-    return nqt == 2 ? launch_prefill_d<128, 2>(hm, uf, mk, mv, a, grid, st)
-                    : launch_prefill_d<128, 1>(hm, uf, mk, mv, a, grid, st);
+        return nqt == 2 ? launch_prefill_d<64, 2>(hm, uf, mk, mv, mo, a, grid, st)
+                        : launch_prefill_d<64, 1>(hm, uf, mk, mv, mo, a, grid, st);
+    return nqt == 2 ? launch_prefill_d<128, 2>(hm, uf, mk, mv, mo, a, grid, st)
+                    : launch_prefill_d<128, 1>(hm, uf, mk, mv, mo, a, grid, st);
 }
 
 size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, int sms) {
@@ -498,8 +521,12 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         a.causal = params->causal; a.window = params->window;
         a.q_quant8 = g.kv_type == VTX_TYPE_Q8_0;
         a.err = ds->err;
+        CUtensorMap mo;
+        std::memset(&mo, 0, sizeof(mo));
+        a.o_tma = encode_out_map(&mo, dst->data, g.D, g.Hq, g.n_q, g.B, dst->nb[1], dst->nb[2], dst->nb[3], g.G,
+                                 pp.tok_per_tile) == VTX_OK;
         dim3 grid(pp.n_cta_q, g.Hkv, g.B);
-        return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, a, grid, st);
+        return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, mo, a, grid, st);
     }
 
     // ---- split-KV path ---------------------------------------------------------

@@ -91,6 +91,18 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const void *desc, uint64_
         : "memory");
 }
 
+// 4-D tiled store shared -> global (bulk async group).  x * element size must
+// be a multiple of 16 bytes and no coordinate may be negative; boxes that
+// reach past the tensor's extent are clipped by the hardware.
+__device__ __forceinline__ void tma_store_4d(const void *desc, const void *src, int x, int y, int z, int w) {
+    asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(desc),
+                 "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z), "r"(w)
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until every committed bulk store has finished READING shared memory
+__device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // ---- tcgen05: TMEM ----------------------------------------------------------
 // Allocate `ncols` TMEM columns (power of two >= 32); the base address is
 // written to shared memory at `dst`.  Executed by one full warp.
