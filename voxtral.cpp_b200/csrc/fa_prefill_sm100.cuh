@@ -67,21 +67,29 @@ template <int D, int NQT> struct PrefillCfg {
     static constexpr int Q_OFF = 0;
     static constexpr int K_OFF = Q_OFF + NQT * TILE_BYTES;
     static constexpr int V_OFF = K_OFF + STAGES * TILE_BYTES;
-    static constexpr int BAR_OFF = V_OFF + STAGES * TILE_BYTES;
+    // Row sums by the tensor core (D = 64): the P V product runs with N = D + 16,
+    // the extra 16 columns of "V" being a constant block whose first column is
+    // 1, so O column D accumulates sum_j P_ij and the softmax warps spend no
+    // adds on it.  The block follows the V ring and is reached through the
+    // descriptor's leading-byte offset (the distance between 64-column blocks).
+    static constexpr bool ROWSUM = D == 64;
+    static constexpr int OC = D + (ROWSUM ? 16 : 0);          // O accumulator columns
+    static constexpr int ONES_OFF = V_OFF + STAGES * TILE_BYTES;
+    static constexpr int BAR_OFF = ONES_OFF + (ROWSUM ? 16384 : 0);
     // Look-ahead (LA): when every tile can own S (128 columns), P (64) and O
     // (D) in TMEM, P gets its own columns and Q K^T of the next key tile runs
     // while the softmax of the current one is still computing.  Otherwise P
     // aliases S and the next S waits for P V.
-    static constexpr bool LA = NQT * (128 + 64 + D) <= 512;
+    static constexpr bool LA = !ROWSUM && NQT * (128 + 64 + D) <= 512;
     static constexpr int NBARS = 1 + 2 * STAGES + 4 * NQT + 1;
     static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;   // +1024 alignment slack
     static constexpr int NTHREADS = 128 * NQT + 128;
     static constexpr int TMA_WARP = 4 * NQT, MMA_WARP = 4 * NQT + 1;
-    static constexpr int TMEM_USED = LA ? NQT * (192 + D) : NQT * (128 + D);
+    static constexpr int TMEM_USED = LA ? NQT * (192 + D) : NQT * (128 + OC);
     static constexpr int TMEM_COLS = TMEM_USED <= 256 ? 256 : 512;
     __host__ __device__ static constexpr int s_col(int t) { return LA ? t * (192 + D) : t * 128; }
     __host__ __device__ static constexpr int p_col(int t) { return LA ? s_col(t) + 128 : s_col(t); }
-    __host__ __device__ static constexpr int o_col(int t) { return LA ? s_col(t) + 192 : NQT * 128 + t * D; }
+    __host__ __device__ static constexpr int o_col(int t) { return LA ? s_col(t) + 192 : NQT * 128 + t * OC; }
     // register split (NQT = 2: 384 threads launched at 168 registers)
     static constexpr int REG_SOFTMAX = 224, REG_PRODUCER = 56;
     // out of every 8 column pairs, POLY_PAIRS use the FMA-pipe exp2
@@ -224,6 +232,17 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     if (warp == C::TMA_WARP && lane == 0) {
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+    }
+    if constexpr (C::ROWSUM) {
+        // constant block [128 keys][64 columns] f16 in the V tiles' 128-byte
+        // swizzled layout: column 0 is 1.0 (16-byte chunk 0 of key row k sits at
+        // chunk k & 7), everything else 0
+        for (int i = tid; i < 1024; i += C::NTHREADS) {
+            const int k = i >> 3, pos = i & 7;
+            *reinterpret_cast<uint4 *>(smem + C::ONES_OFF + i * 16) =
+                make_uint4(pos == (k & 7) ? 0x3C00u : 0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
     }
     tc_fence_before();
     __syncthreads();
@@ -404,9 +423,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 }
                 s[2 * pi] = e0;
                 s[2 * pi + 1] = e1;
-                sum2[pi & 3] = fadd2(sum2[pi & 3], pk2(e0, e1));
+                if (!C::ROWSUM) sum2[pi & 3] = fadd2(sum2[pi & 3], pk2(e0, e1));
             }
-            {
+            if (!C::ROWSUM) {
                 const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
                 float sa, sb;
                 upk2(s01, sa, sb);
@@ -436,6 +455,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
                     tmem_st32(o_addr + c * 32, o);
                 }
+                if constexpr (C::ROWSUM) {            // the row-sum column (columns D+1.. stay 0)
+                    uint32_t l1 = tmem_ld1(o_addr + D);
+                    tmem_ld_wait();
+                    tmem_st1(o_addr + D, __float_as_uint(__uint_as_float(l1) * alpha));
+                }
             }
             tmem_st_wait();
             tc_fence_before();
@@ -456,6 +480,12 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             char *st = smem + C::Q_OFF + t * (D / 32) * 16384;
             if (ok) {
                 tc_fence_after();
+                if constexpr (C::ROWSUM) {
+                    if (n_iter > 0) {
+                        l_run = __uint_as_float(tmem_ld1(o_addr + D));
+                        tmem_ld_wait();
+                    }
+                }
                 const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
@@ -492,6 +522,12 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             float *stage = reinterpret_cast<float *>(smem + C::Q_OFF) + t * 128 * OP;
             if (ok) {
                 tc_fence_after();
+                if constexpr (C::ROWSUM) {
+                    if (n_iter > 0) {
+                        l_run = __uint_as_float(tmem_ld1(o_addr + D));
+                        tmem_ld_wait();
+                    }
+                }
                 const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
@@ -575,7 +611,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (n_iter > 0) {
                 const uint32_t lead = elect_one();     // the warp stays converged
                 constexpr uint32_t IDESC_QK = idesc_f16_f32(128, 128, 0, 0);
-                constexpr uint32_t IDESC_PV = idesc_f16_f32(128, D, 0, 1);
+                constexpr uint32_t IDESC_PV = idesc_f16_f32(128, C::OC, 0, 1);
                 constexpr uint32_t HI = (1024u >> 4) | (1u << 14) | (2u << 29);   // SBO 1024, v1, SW128
                 const uint32_t sbase = smem_u32(smem);
                 const uint32_t lo_q = ((sbase + C::Q_OFF) >> 4) | (1u << 16);          // LBO 16 B (K-major)
@@ -601,7 +637,10 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 auto issue_pv = [&](int t, int vst, uint32_t acc) {
                     const uint32_t p_tm = tmem + C::p_col(t);
                     const uint32_t o_tm = tmem + C::o_col(t);
-                    const uint32_t v_lo = lo_v + vst * T16;
+                    // ROWSUM: the leading-byte offset reaches the constant block after the V ring
+                    const uint32_t v_lo = C::ROWSUM ? (((sbase + C::V_OFF) >> 4) + vst * T16) |
+                                                          (((uint32_t)(C::ONES_OFF - C::V_OFF) / 16u - vst * T16) << 16)
+                                                    : lo_v + vst * T16;
                     mma_f16_ts_w(lead, o_tm, p_tm, desc64(v_lo, HI), IDESC_PV, acc);
 #pragma unroll
                     for (int kk = 1; kk < 8; ++kk)
