@@ -322,12 +322,25 @@ def run_decode(args, rank, world, local):
     lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
     g = torch.Generator(device=dev)
     g.manual_seed(77 + rank)
-    ks, vs = [], []
-    for L in lens:
-        ks.append(torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16))
-        vs.append(torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16))
-    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D, vtx_attn.F16,
-                                    Hkv * D * 2, D * 2, int(lens.max()), 1.0 / D ** 0.5)
+    q8 = getattr(args, "kv", "f16") == "q8_0"
+    row = D // 32 * 34 if q8 else D * 2                   # bytes of one head's K (or V) row
+
+    def cache(L):
+        if not q8:
+            return torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16)
+        # ggml Q8_0 blocks {f16 d; int8 qs[32]}: qs ~ U[-127, 127], d ~ U[0.005, 0.05]
+        blk = torch.empty((int(L), Hkv, D // 32, 34), dtype=torch.uint8, device=dev)
+        blk[..., 2:] = torch.randint(-127, 128, blk[..., 2:].shape, generator=g, device=dev,
+                                     dtype=torch.int16).to(torch.int8).view(torch.uint8)
+        d = (torch.rand(blk.shape[:-1], generator=g, device=dev) * 0.045 + 0.005).to(torch.float16)
+        blk[..., :2] = d.unsqueeze(-1).view(torch.uint8).reshape(*blk.shape[:-1], 2)
+        return blk
+
+    ks = [cache(L) for L in lens]
+    vs = [cache(L) for L in lens]
+    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D,
+                                    vtx_attn.Q8_0 if q8 else vtx_attn.F16, Hkv * row, row, int(lens.max()),
+                                    1.0 / D ** 0.5)
     q = torch.randn((S, Hq, D), generator=g, device=dev)
     out = torch.empty_like(q)
     stream = torch.cuda.Stream(device=dev)
@@ -346,16 +359,18 @@ def run_decode(args, rank, world, local):
         barrier(world)
     ms_local = e0.elapsed_time(e1)
     ms = barrier_max(ms_local, world)
-    kv_bytes = float(lens.astype(np.int64).sum()) * Hkv * D * 2 * 2
+    kv_bytes = float(lens.astype(np.int64).sum()) * Hkv * row * 2
     value = kv_bytes * args.steps * world / (ms * 1e-3) / 1e9
     peaks = load_peaks()
     achieved = kv_bytes / (ms_local / args.steps * 1e-3) / 1e9
     return {
         "metric": METRIC_DEC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
-        "data": "synthetic N(0,1) f16 KV, ragged lengths U[512,16384] seeded per rank",
-        "config": {"workload": "configs[4] batched decode: 256 streams, GQA 32/8 x 128, f16 KV, 1 layer per step",
+        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0" if q8 else "f16",
+        "data": ("synthetic Q8_0 KV (int8 U[-127,127], f16 scales)" if q8 else "synthetic N(0,1) f16 KV")
+                + ", ragged lengths U[512,16384] seeded per rank",
+        "config": {"workload": f"configs[4] batched decode: {S} streams, GQA 32/8 x 128, "
+                               f"{'Q8_0' if q8 else 'f16'} KV, 1 layer per step",
                    "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.1f} GB KV per step)",
                    "parallelism": f"dp{world} (independent streams per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -403,6 +418,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
+    ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="decode workload: KV cache type")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 

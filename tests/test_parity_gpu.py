@@ -189,6 +189,29 @@ def test_decode_batched_ragged(kv):
     assert_close(got.cpu().numpy(), ref, f"batched decode {kv}")
 
 
+@pytest.mark.parametrize("Hkv", [2, 4])
+def test_decode_batched_q8_0_head_groups(Hkv):
+    """Q8_0 streaming decode with fewer than 8 KV heads per token row (one CTA
+    copies 2 or 4 heads' slices), G = 4, lengths that need several splits."""
+    import vtx_attn
+    rng = np.random.default_rng(30 + Hkv)
+    n_seq, D = 5, 128
+    Hq = 4 * Hkv
+    lens = np.array([1, 17, 1024, 2049, 4500], dtype=np.int32)
+    qn = rng.standard_normal((n_seq, Hq, D)).astype(np.float32)
+    ks = [O.quantize_q8_0(rng.standard_normal((int(L), Hkv, D)).astype(np.float32)) for L in lens]
+    vs = [O.quantize_q8_0(rng.standard_normal((int(L), Hkv, D)).astype(np.float32)) for L in lens]
+    row, nb2 = ks[0].strides[0], ks[0].strides[1]
+    ref = O.decode_batched(qn, ks, vs, lens, 1 / np.sqrt(D), O.Q8_0, Hkv, row, nb2)
+    plan = vtx_attn.DecodeBatchPlan([torch.from_numpy(a).cuda() for a in ks], [torch.from_numpy(a).cuda() for a in vs],
+                                    torch.from_numpy(lens).cuda(), Hq, Hkv, D, O.Q8_0, row, nb2, int(lens.max()),
+                                    float(1 / np.sqrt(D)))
+    got = plan(torch.from_numpy(qn).cuda())
+    torch.cuda.synchronize()
+    assert vtx_attn.read_device_error() == 0
+    assert_close(got.cpu().numpy(), ref, f"batched q8_0 decode Hkv={Hkv}")
+
+
 # ---- error paths through the C ABI ---------------------------------------------
 
 def test_errors_are_status_codes():

@@ -67,6 +67,98 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+// One step of 16 keys for one warp: S = Q K^T (rows = the G query heads of
+// the group, keys in two 8-wide halves), online softmax of this lane's row
+// (lazy rescale), O += P V.  ks / vs: 16 rows of D halves at byte pitch
+// PITCH (rows >= n hold zeros); qa: the Q A-fragments; cx = scale * log2(e).
+template <int D, int PITCH>
+__device__ __forceinline__ void decode_tile(const char *ks, const char *vs, int n, const uint32_t (&qa)[D / 16][4],
+                                            float cx, float (&o)[D / 8][4], float &m_run, float &l_part, int lane)
+{
+    constexpr int KC = D / 16, NB = D / 8;
+    const int lrow = lane & 7, lmat = lane >> 3;    // ldmatrix: lane -> (row within 8x8, matrix)
+    // S (16 rows x 16 keys) as two 16x8 accumulators
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kc = 0; kc < KC; kc += 2) {
+        // matrices: keys 0-7 x dims [16kc, +8), [+8, +16), [+16, +24), [+24, +32)
+        uint32_t bk[4], bk2[4];
+        ldsm_x4(bk, ks + lrow * PITCH + (kc * 16 + lmat * 8) * 2);
+        ldsm_x4(bk2, ks + (8 + lrow) * PITCH + (kc * 16 + lmat * 8) * 2);
+        mma16816(s0, qa[kc], bk[0], bk[1]);
+        mma16816(s1, qa[kc], bk2[0], bk2[1]);
+        mma16816(s0, qa[kc + 1], bk[2], bk[3]);
+        mma16816(s1, qa[kc + 1], bk2[2], bk2[3]);
+    }
+    // this lane's row: keys 2(l%4)+{0,1} (s0) and 8+2(l%4)+{0,1} (s1)
+    const int kk = 2 * (lane & 3);
+    float x[4] = {s0[0] * cx, s0[1] * cx, s1[0] * cx, s1[1] * cx};
+    if (n < 16) {
+        if (kk >= n) x[0] = -INFINITY;
+        if (kk + 1 >= n) x[1] = -INFINITY;
+        if (kk + 8 >= n) x[2] = -INFINITY;
+        if (kk + 9 >= n) x[3] = -INFINITY;
+    }
+    float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    if (mx > m_run + 8.0f) {                        // lazy rescale, uniform within the quad
+        const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mx);
+        m_run = mx;
+        l_part *= alpha;
+#pragma unroll
+        for (int i = 0; i < NB; ++i) { o[i][0] *= alpha; o[i][1] *= alpha; }
+    }
+    const float mu = m_run == -INFINITY ? 0.f : m_run;
+    const float p0 = ex2(x[0] - mu), p1 = ex2(x[1] - mu), p2 = ex2(x[2] - mu), p3 = ex2(x[3] - mu);
+    l_part += (p0 + p1) + (p2 + p3);
+    // P as the A fragment of the PV product (rows 8..15 zero)
+    const uint32_t pa[4] = {pack_half2(p0, p1), 0u, pack_half2(p2, p3), 0u};
+    // O (16 x D) += P (16 x 16 keys) V (16 keys x D): B fragments by ldmatrix.trans
+#pragma unroll
+    for (int nb = 0; nb < NB; nb += 2) {
+        // matrices: keys 0-7 / 8-15 x dims [8nb, +8), [8nb+8, +16)
+        uint32_t bv[4];
+        ldsm_x4_t(bv, vs + ((lmat & 1) * 8 + lrow) * PITCH + (nb * 8 + (lmat >> 1) * 8) * 2);
+        mma16816(o[nb], pa, bv[0], bv[1]);
+        mma16816(o[nb + 1], pa, bv[2], bv[3]);
+    }
+}
+
+// Writes one lane's share of a (G x D) result: the final normalised rows
+// (write_final) or the split's partial (O, m, l) in the combine layout.
+template <int D>
+__device__ __forceinline__ void decode_store(const SplitArgs &a, int b, int g, int sp, const float (&o)[D / 8][4],
+                                             float m_run, float l_part, int lane)
+{
+    constexpr int NB = D / 8;
+    const int qrow = lane >> 2;
+    float l = l_part;
+    l += __shfl_xor_sync(0xffffffffu, l, 1);
+    l += __shfl_xor_sync(0xffffffffu, l, 2);
+    if (qrow < a.G) {
+        const int h = g * a.G + qrow;
+        const int kk = 2 * (lane & 3);              // this lane's output columns within each 8-block
+        const long long work = ((long long)b * a.Hkv + g) * a.n_splits + sp;   // n_qtiles = n_hchunks = 1
+        if (a.write_final) {
+            float *out = reinterpret_cast<float *>(a.dst + (long long)h * a.d_nb1 + (long long)b * a.d_nb3);
+            const float inv = l == 0.f ? 0.f : 1.f / l;
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+                *reinterpret_cast<float2 *>(out + nb * 8 + kk) = make_float2(o[nb][0] * inv, o[nb][1] * inv);
+        } else {
+            float *po = a.part_o + (work * 4 + qrow) * D;
+#pragma unroll
+            for (int nb = 0; nb < NB; ++nb)
+                *reinterpret_cast<float2 *>(po + nb * 8 + kk) = make_float2(o[nb][0], o[nb][1]);
+            if ((lane & 3) == 0) {
+                a.part_ml[(work * 4 + qrow) * 2 + 0] = m_run;
+                a.part_ml[(work * 4 + qrow) * 2 + 1] = l;
+            }
+        }
+    }
+}
+
 template <int D>
 __global__ void __launch_bounds__(128, 2)
 fa_decode_mma_kernel(const SplitArgs a, int n_items)
@@ -177,7 +269,6 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
     for (int i = 0; i < NB; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_part = 0.f;         // this lane's row (qrow), partial sum
     const float cx = a.qk_scale * kLog2e;
-    const int lrow = lane & 7, lmat = lane >> 3;    // ldmatrix: lane -> (row within 8x8, matrix)
     bool ok = true;
     int t_done = 0;
 
@@ -188,54 +279,7 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
         const char *ks = ring + stg * C::STAGE_BYTES;
         const char *vs = ks + C::KEYS * C::PITCH;
         const int k0 = kb + t * C::KEYS;
-        const int n = min(C::KEYS, ke - k0);
-
-        // S (16 rows x 16 keys) as two 16x8 accumulators
-        float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-        for (int kc = 0; kc < KC; kc += 2) {
-            // matrices: keys 0-7 x dims [16kc, +8), [+8, +16), [+16, +24), [+24, +32)
-            uint32_t bk[4], bk2[4];
-            ldsm_x4(bk, ks + lrow * C::PITCH + (kc * 16 + lmat * 8) * 2);
-            ldsm_x4(bk2, ks + (8 + lrow) * C::PITCH + (kc * 16 + lmat * 8) * 2);
-            mma16816(s0, qa[kc], bk[0], bk[1]);
-            mma16816(s1, qa[kc], bk2[0], bk2[1]);
-            mma16816(s0, qa[kc + 1], bk[2], bk[3]);
-            mma16816(s1, qa[kc + 1], bk2[2], bk2[3]);
-        }
-        // this lane's row: keys 2(l%4)+{0,1} (s0) and 8+2(l%4)+{0,1} (s1)
-        const int kk = 2 * (lane & 3);
-        float x[4] = {s0[0] * cx, s0[1] * cx, s1[0] * cx, s1[1] * cx};
-        if (n < C::KEYS) {
-            if (kk >= n) x[0] = -INFINITY;
-            if (kk + 1 >= n) x[1] = -INFINITY;
-            if (kk + 8 >= n) x[2] = -INFINITY;
-            if (kk + 9 >= n) x[3] = -INFINITY;
-        }
-        float mx = fmaxf(fmaxf(x[0], x[1]), fmaxf(x[2], x[3]));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-        if (mx > m_run + 8.0f) {                    // lazy rescale, uniform within the quad
-            const float alpha = m_run == -INFINITY ? 0.f : ex2(m_run - mx);
-            m_run = mx;
-            l_part *= alpha;
-#pragma unroll
-            for (int i = 0; i < NB; ++i) { o[i][0] *= alpha; o[i][1] *= alpha; }
-        }
-        const float mu = m_run == -INFINITY ? 0.f : m_run;
-        const float p0 = ex2(x[0] - mu), p1 = ex2(x[1] - mu), p2 = ex2(x[2] - mu), p3 = ex2(x[3] - mu);
-        l_part += (p0 + p1) + (p2 + p3);
-        // P as the A fragment of the PV product (rows 8..15 zero)
-        const uint32_t pa[4] = {pack_half2(p0, p1), 0u, pack_half2(p2, p3), 0u};
-        // O (16 x D) += P (16 x 16 keys) V (16 keys x D): B fragments by ldmatrix.trans
-#pragma unroll
-        for (int nb = 0; nb < NB; nb += 2) {
-            // matrices: keys 0-7 / 8-15 x dims [8nb, +8), [8nb+8, +16)
-            uint32_t bv[4];
-            ldsm_x4_t(bv, vs + ((lmat & 1) * 8 + lrow) * C::PITCH + (nb * 8 + (lmat >> 1) * 8) * 2);
-            mma16816(o[nb], pa, bv[0], bv[1]);
-            mma16816(o[nb + 1], pa, bv[2], bv[3]);
-        }
+        decode_tile<D, C::PITCH>(ks, vs, min(C::KEYS, ke - k0), qa, cx, o, m_run, l_part, lane);
         __syncwarp();                               // every lane has read this stage
         issue(t + C::STAGES);
         t_done = t + 1;
@@ -245,30 +289,7 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
         mbar_wait(&full[t % C::STAGES], (t / C::STAGES) & 1, nullptr, 0);
 
     // ---- write the partial (or the final row) ---------------------------------
-    float l = l_part;
-    l += __shfl_xor_sync(0xffffffffu, l, 1);
-    l += __shfl_xor_sync(0xffffffffu, l, 2);
-    if (qrow < a.G) {
-        const int h = g * a.G + qrow;
-        const int kk = 2 * (lane & 3);              // this lane's output columns within each 8-block
-        const long long work = ((long long)b * a.Hkv + g) * a.n_splits + sp;   // n_qtiles = n_hchunks = 1
-        if (a.write_final) {
-            float *out = reinterpret_cast<float *>(a.dst + (long long)h * a.d_nb1 + (long long)b * a.d_nb3);
-            const float inv = l == 0.f ? 0.f : 1.f / l;
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb)
-                *reinterpret_cast<float2 *>(out + nb * 8 + kk) = make_float2(o[nb][0] * inv, o[nb][1] * inv);
-        } else {
-            float *po = a.part_o + (work * 4 + qrow) * D;
-#pragma unroll
-            for (int nb = 0; nb < NB; ++nb)
-                *reinterpret_cast<float2 *>(po + nb * 8 + kk) = make_float2(o[nb][0], o[nb][1]);
-            if ((lane & 3) == 0) {
-                a.part_ml[(work * 4 + qrow) * 2 + 0] = m_run;
-                a.part_ml[(work * 4 + qrow) * 2 + 1] = l;
-            }
-        }
-    }
+    decode_store<D>(a, b, g, sp, o, m_run, l_part, lane);
 }
 
 }  // namespace vtx

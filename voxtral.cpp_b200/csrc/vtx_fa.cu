@@ -25,6 +25,7 @@
 #include "fa_splitkv.cuh"
 #include "fa_prefill_sm100.cuh"
 #include "fa_decode_mma.cuh"
+#include "fa_decode_q8.cuh"
 
 using namespace vtx;
 
@@ -349,6 +350,43 @@ int launch_decode_mma(const SplitArgs &a, int D, cudaStream_t st) {
     return D == 64 ? launch_decode_mma_t<64>(a, st) : launch_decode_mma_t<128>(a, st);
 }
 
+// Q8_0 streaming decode: one CTA per (stream, group of hpc KV heads, key
+// split); the heads' slices of a token row are copied as one contiguous span,
+// so heads must be adjacent in the row (nb2 = one head's 136-byte row) and the
+// span a multiple of 16 bytes (hpc even).  Returns hpc, or 0 when unusable.
+int decode_q8_hpc(int kv_type, int D, int n_q, int G, int Hkv, int maxr, int n_hchunks, long long k_nb1,
+                  long long k_nb2, long long v_nb1, long long v_nb2) {
+    if (kv_type != VTX_TYPE_Q8_0 || D != 128 || n_q != 1 || G > 4 || maxr != 4 || n_hchunks != 1) return 0;
+    constexpr int BLK = DecodeQ8Cfg<128>::BLK;
+    if ((Hkv > 1 && (k_nb2 != BLK || v_nb2 != BLK)) || k_nb1 % 16 || v_nb1 % 16) return 0;
+    for (int h = std::min(Hkv, DecodeQ8Cfg<128>::HPC_MAX); h >= 2; --h)
+        if (Hkv % h == 0 && (h * BLK) % 16 == 0) return h;
+    return 0;
+}
+
+int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
+    using C = DecodeQ8Cfg<128>;
+    static int attr_done[kMaxDevices] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(fa_decode_q8_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev] = 1;
+    }
+    const long long items = (long long)a.B * (a.Hkv / hpc) * a.n_splits;
+    if (items > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
+    fa_decode_q8_kernel<128><<<(unsigned)items, C::NTHREADS, C::SMEM, st>>>(a, hpc);
+    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (!a.write_final) {
+        const long long rows = (long long)a.B * a.Hkv * a.G;
+        fa_combine_kernel<128, 4><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, a.Hkv);
+        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    }
+    return VTX_OK;
+}
+
 bool decode_mma_ok(int kv_type, int n_q, int G, int vec, int maxr, int n_hchunks) {
     return kv_type == VTX_TYPE_F16 && n_q == 1 && G <= 4 && vec == 16 && maxr == 4 && n_hchunks == 1;
 }
@@ -570,6 +608,13 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
     if (decode_mma_ok(g.kv_type, g.n_q, g.G, a.vec, sp.maxr, sp.n_hchunks) && !mask && !params->causal &&
         params->logit_softcap == 0.0f)
         return launch_decode_mma(a, g.D, st);
+    if (!mask && !params->causal && params->logit_softcap == 0.0f) {
+        const int hpc = decode_q8_hpc(g.kv_type, g.D, g.n_q, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
+                                      a.v_nb1, a.v_nb2);
+        const uintptr_t bases = reinterpret_cast<uintptr_t>(a.k) | reinterpret_cast<uintptr_t>(a.v) |
+                                (uintptr_t)a.k_nb3 | (uintptr_t)a.v_nb3;
+        if (hpc && bases % 16 == 0) return launch_decode_q8(a, hpc, st);
+    }
     dim3 grid((unsigned)(sp.n_splits * sp.n_qtiles), (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)g.B);
     return launch_split(a, g.D, g.kv_type, sp.maxr, grid, st);
 }
@@ -634,6 +679,9 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
     a.err = ds->err;
     if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
         return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
+    if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
+                                      a.v_nb1, a.v_nb2))
+        return launch_decode_q8(a, hpc, static_cast<cudaStream_t>(stream));
     dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
     return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
 }
@@ -744,6 +792,9 @@ extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, 
     a.err = ds->err;
     if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
         return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
+    if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
+                                      a.v_nb1, a.v_nb2))
+        return launch_decode_q8(a, hpc, static_cast<cudaStream_t>(stream));
     dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
     return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
 }
