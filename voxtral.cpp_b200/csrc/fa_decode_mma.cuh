@@ -67,29 +67,21 @@ __device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
-// One step of 16 keys for one warp: S = Q K^T (rows = the G query heads of
-// the group, keys in two 8-wide halves), online softmax of this lane's row
-// (lazy rescale), O += P V.  ks / vs: 16 rows of D halves at byte pitch
-// PITCH (rows >= n hold zeros); qa: the Q A-fragments; cx = scale * log2(e).
-template <int D, int PITCH>
-__device__ __forceinline__ void decode_tile(const char *ks, const char *vs, int n, const uint32_t (&qa)[D / 16][4],
-                                            float cx, float (&o)[D / 8][4], float &m_run, float &l_part, int lane)
+// One step of 16 keys for one warp, in two halves so that K and V can share
+// one staging tile.  decode_scores: S = Q K^T (rows = the G query heads of the
+// group, keys in two 8-wide halves), online softmax of this lane's row (lazy
+// rescale of O), P packed as the A fragment of the PV product.  decode_pv:
+// O += P V.  ks / vs: 16 rows of D halves at byte pitch PITCH (rows >= n hold
+// zeros); qa: the Q A-fragments; cx = scale * log2(e).
+// Online softmax of this lane's row of S (16 rows x 16 keys held as two 16x8
+// accumulators s0 = keys 0-7, s1 = keys 8-15): lazy rescale of O, P packed
+// as the A fragment of the PV product.
+template <int D>
+__device__ __forceinline__ void decode_softmax(const float (&s0)[4], const float (&s1)[4], int n, float cx,
+                                               float (&o)[D / 8][4], float &m_run, float &l_part, int lane,
+                                               uint32_t (&pa)[4])
 {
-    constexpr int KC = D / 16, NB = D / 8;
-    const int lrow = lane & 7, lmat = lane >> 3;    // ldmatrix: lane -> (row within 8x8, matrix)
-    // S (16 rows x 16 keys) as two 16x8 accumulators
-    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-    for (int kc = 0; kc < KC; kc += 2) {
-        // matrices: keys 0-7 x dims [16kc, +8), [+8, +16), [+16, +24), [+24, +32)
-        uint32_t bk[4], bk2[4];
-        ldsm_x4(bk, ks + lrow * PITCH + (kc * 16 + lmat * 8) * 2);
-        ldsm_x4(bk2, ks + (8 + lrow) * PITCH + (kc * 16 + lmat * 8) * 2);
-        mma16816(s0, qa[kc], bk[0], bk[1]);
-        mma16816(s1, qa[kc], bk2[0], bk2[1]);
-        mma16816(s0, qa[kc + 1], bk[2], bk[3]);
-        mma16816(s1, qa[kc + 1], bk2[2], bk2[3]);
-    }
+    constexpr int NB = D / 8;
     // this lane's row: keys 2(l%4)+{0,1} (s0) and 8+2(l%4)+{0,1} (s1)
     const int kk = 2 * (lane & 3);
     float x[4] = {s0[0] * cx, s0[1] * cx, s1[0] * cx, s1[1] * cx};
@@ -113,7 +105,48 @@ __device__ __forceinline__ void decode_tile(const char *ks, const char *vs, int 
     const float p0 = ex2(x[0] - mu), p1 = ex2(x[1] - mu), p2 = ex2(x[2] - mu), p3 = ex2(x[3] - mu);
     l_part += (p0 + p1) + (p2 + p3);
     // P as the A fragment of the PV product (rows 8..15 zero)
-    const uint32_t pa[4] = {pack_half2(p0, p1), 0u, pack_half2(p2, p3), 0u};
+    pa[0] = pack_half2(p0, p1);
+    pa[1] = 0u;
+    pa[2] = pack_half2(p2, p3);
+    pa[3] = 0u;
+}
+
+// S = Q K^T for 16 keys (rows = the G query heads of the group) from K rows in
+// shared memory (ldmatrix), then decode_softmax.  Even and odd dim chunks
+// accumulate in separate chains (half the dependent-MMA latency).
+template <int D, int PITCH>
+__device__ __forceinline__ void decode_scores(const char *ks, int n, const uint32_t (&qa)[D / 16][4], float cx,
+                                              float (&o)[D / 8][4], float &m_run, float &l_part, int lane,
+                                              uint32_t (&pa)[4])
+{
+    constexpr int KC = D / 16;
+    const int lrow = lane & 7, lmat = lane >> 3;    // ldmatrix: lane -> (row within 8x8, matrix)
+    float s0[4] = {0.f, 0.f, 0.f, 0.f}, s1[4] = {0.f, 0.f, 0.f, 0.f};
+    float e0[4] = {0.f, 0.f, 0.f, 0.f}, e1[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int kc = 0; kc < KC; kc += 2) {
+        // matrices: keys 0-7 x dims [16kc, +8), [+8, +16), [+16, +24), [+24, +32)
+        uint32_t bk[4], bk2[4];
+        ldsm_x4(bk, ks + lrow * PITCH + (kc * 16 + lmat * 8) * 2);
+        ldsm_x4(bk2, ks + (8 + lrow) * PITCH + (kc * 16 + lmat * 8) * 2);
+        mma16816(s0, qa[kc], bk[0], bk[1]);
+        mma16816(s1, qa[kc], bk2[0], bk2[1]);
+        mma16816(e0, qa[kc + 1], bk[2], bk[3]);
+        mma16816(e1, qa[kc + 1], bk2[2], bk2[3]);
+    }
+#pragma unroll
+    for (int i = 0; i < 2; ++i) {
+        s0[i] += e0[i];
+        s1[i] += e1[i];
+    }
+    decode_softmax<D>(s0, s1, n, cx, o, m_run, l_part, lane, pa);
+}
+
+template <int D, int PITCH>
+__device__ __forceinline__ void decode_pv(const char *vs, const uint32_t (&pa)[4], float (&o)[D / 8][4], int lane)
+{
+    constexpr int NB = D / 8;
+    const int lrow = lane & 7, lmat = lane >> 3;
     // O (16 x D) += P (16 x 16 keys) V (16 keys x D): B fragments by ldmatrix.trans
 #pragma unroll
     for (int nb = 0; nb < NB; nb += 2) {
@@ -123,6 +156,15 @@ __device__ __forceinline__ void decode_tile(const char *ks, const char *vs, int 
         mma16816(o[nb], pa, bv[0], bv[1]);
         mma16816(o[nb + 1], pa, bv[2], bv[3]);
     }
+}
+
+template <int D, int PITCH>
+__device__ __forceinline__ void decode_tile(const char *ks, const char *vs, int n, const uint32_t (&qa)[D / 16][4],
+                                            float cx, float (&o)[D / 8][4], float &m_run, float &l_part, int lane)
+{
+    uint32_t pa[4];
+    decode_scores<D, PITCH>(ks, n, qa, cx, o, m_run, l_part, lane, pa);
+    decode_pv<D, PITCH>(vs, pa, o, lane);
 }
 
 // Writes one lane's share of a (G x D) result: the final normalised rows

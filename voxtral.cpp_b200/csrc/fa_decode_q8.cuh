@@ -13,15 +13,17 @@
 //                   3-stage ring — HPC * 136 bytes, contiguous and 16-byte
 //                   aligned; completion counted by one mbarrier per stage,
 //                   reuse gated by a second one (one arrival per head warp).
-//   warp w < HPC    head h0 + w: dequantises its K and V slices of the stage
-//                   into a private f16 tile (lane l: K row l or V row l - 16,
-//                   17 8-byte loads; ring rows are padded by 16 B so the 16
-//                   lanes of a half-warp meet at most 2 to a bank: int8 -> f16
-//                   exactly through the 0x64xx bit pattern, then times the
-//                   block scale, rounded once to f16), then
-//                   runs the same tensor-core step as the F16 kernel
-//                   (decode_tile): S = Q K^T with the G query heads as the M
-//                   rows, online softmax, O += P V.
+//   warp w < HPC    head h0 + w: dequantises its K slices of the stage into
+//                   a private f16 tile (two lanes per key, 68 bytes = two
+//                   blocks each; ring rows are padded by 16 B so the lanes
+//                   meet at most 2 to a bank; int8 -> f16 exactly through the
+//                   0x64xx bit pattern, then times the block scale, rounded
+//                   once to f16), computes S = Q K^T and the softmax on the
+//                   tensor core (decode_scores, the F16 kernel's step, G
+//                   query heads as the M rows), then dequantises V into the
+//                   same tile, releases the ring stage and adds P V.  One
+//                   tile per warp leaves room for a 5-stage ring, so ~140 KB
+//                   of a CTA's rows are in flight.
 //
 // Q is quantised to Q8_0 per 32 values first, as ggml's CPU kernel does before
 // its Q8_0 dot (d = amax/127, q = round-half-even(x * 127/amax)), and fed to
@@ -38,12 +40,12 @@ namespace vtx {
 template <int D> struct DecodeQ8Cfg {
     static_assert(D == 128, "Q8_0 streaming decode is built for head_dim 128");
     static constexpr int KEYS = 16;                          // keys per stage
-    static constexpr int STAGES = 3;
+    static constexpr int STAGES = 5;                         // ~140 KB of a CTA's rows in flight
     static constexpr int HPC_MAX = 8;                        // KV heads per CTA (= head warps)
     static constexpr int BLK = D / 32 * 34;                  // one head's Q8_0 row (136 B)
     static constexpr int RING_STAGE = 2 * KEYS * (HPC_MAX * BLK + 16);   // rows padded by 16 B
     static constexpr int FPITCH = D * 2 + 16;                // dequantised f16 row pitch
-    static constexpr int WBUF = 2 * KEYS * FPITCH;           // one head warp's f16 K + V tile
+    static constexpr int WBUF = KEYS * FPITCH;               // one head warp's f16 tile (K, then V)
     static constexpr int BUF_OFF = STAGES * RING_STAGE;
     static constexpr int BAR_OFF = BUF_OFF + HPC_MAX * WBUF;
     static constexpr int SMEM = BAR_OFF + 2 * STAGES * 8;
@@ -65,36 +67,26 @@ __device__ __forceinline__ void q8x4_to_h2(uint32_t w, __half2 d2, uint32_t &lo,
     hi = *reinterpret_cast<uint32_t *>(&fb);
 }
 
-// One head's Q8_0 row (4 blocks, 136 bytes from an 8-byte aligned
-// shared-memory address) -> 128 halves written to dst (16-byte aligned).
-// Blocks 0 and 2 carry their int8 values at a 2-byte offset (funnel shifts),
-// blocks 1 and 3 on word boundaries.
-__device__ __forceinline__ void dequant_row128(const char *src, char *dst) {
-    uint32_t w[34];
+// Half of one head's Q8_0 row: two blocks (68 bytes from a 4-byte aligned
+// shared-memory address) -> 64 halves written to dst (16-byte aligned).
+// The first block's int8 values sit at a 2-byte offset (funnel shifts), the
+// second block's on word boundaries.
+__device__ __forceinline__ void dequant_2blocks(const char *src, char *dst) {
+    uint32_t w[17];
 #pragma unroll
-    for (int i = 0; i < 17; ++i) {
-        const uint2 x = reinterpret_cast<const uint2 *>(src)[i];
-        w[2 * i] = x.x;
-        w[2 * i + 1] = x.y;
+    for (int i = 0; i < 17; ++i) w[i] = reinterpret_cast<const uint32_t *>(src)[i];
+    const __half dA = __ushort_as_half((unsigned short)(w[0] & 0xffffu));   // bytes 0-1
+    const __half dB = __ushort_as_half((unsigned short)(w[8] >> 16));       // bytes 34-35
+    const __half2 dA2 = __halves2half2(dA, dA), dB2 = __halves2half2(dB, dB);
+    uint32_t out[32];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        q8x4_to_h2(__funnelshift_r(w[j], w[j + 1], 16), dA2, out[2 * j], out[2 * j + 1]);   // bytes 2..33
+        q8x4_to_h2(w[9 + j], dB2, out[16 + 2 * j], out[16 + 2 * j + 1]);                  // bytes 36..67
     }
 #pragma unroll
-    for (int blk = 0; blk < 4; ++blk) {
-        const int w0 = blk * 17 / 2;                         // word holding the block's first byte
-        const bool odd = blk & 1;                            // odd blocks start 2 bytes into a word
-        const unsigned short dbits = odd ? (unsigned short)(w[w0] >> 16) : (unsigned short)(w[w0] & 0xffffu);
-        const __half d = __ushort_as_half(dbits);
-        const __half2 d2 = __halves2half2(d, d);
-        uint32_t out[16];
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            const uint32_t q = odd ? w[w0 + 1 + j] : __funnelshift_r(w[w0 + j], w[w0 + j + 1], 16);
-            q8x4_to_h2(q, d2, out[2 * j], out[2 * j + 1]);
-        }
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-            reinterpret_cast<uint4 *>(dst + blk * 64)[i] =
-                make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
-    }
+    for (int i = 0; i < 8; ++i)
+        reinterpret_cast<uint4 *>(dst)[i] = make_uint4(out[4 * i], out[4 * i + 1], out[4 * i + 2], out[4 * i + 3]);
 }
 
 template <int D>
@@ -178,8 +170,7 @@ fa_decode_q8_kernel(const SplitArgs a, int hpc)
 
     // ==================== head warp ============================================
     const int g = hg * hpc + warp;                           // KV head
-    char *wk = smem + C::BUF_OFF + warp * C::WBUF;           // dequantised K tile
-    char *wv = wk + C::KEYS * C::FPITCH;                     // dequantised V tile
+    char *buf = smem + C::BUF_OFF + warp * C::WBUF;          // dequantised K, then V, of a stage
 
     // Q rows of the group as the A fragment (rows >= G are zero), quantised to
     // Q8_0 per 32 values like ggml's from_float for a Q8_0 K
@@ -235,26 +226,33 @@ fa_decode_q8_kernel(const SplitArgs a, int hpc)
     for (int i = 0; i < NB; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
     float m_run = -INFINITY, l_part = 0.f;
     const float cx = a.qk_scale * kLog2e;
-    const int kr = lane & 15;                                // dequant: lane = K row (< 16) or V row
-    char *frow = (lane < 16 ? wk : wv) + kr * C::FPITCH;
+    const int kr = lane >> 1, half = lane & 1;               // dequant: key row, which 2 of its 4 blocks
+    char *frow = buf + kr * C::FPITCH + half * 128;
 
     for (int t = 0; t < ntiles; ++t) {
         const int stg = t % C::STAGES;
         if (!__all_sync(0xffffffffu, mbar_wait(&full[stg], (t / C::STAGES) & 1, a.err, VTX_KERR_KV))) break;
         const int k0 = kb + t * C::KEYS;
         const int n = min(C::KEYS, ke - k0);
-        const char *st = smem + stg * C::RING_STAGE;
-        if (kr < n) {
-            dequant_row128(st + lane * tpitch + warp * C::BLK, frow);
-        } else {
-            // keys past the range were never loaded: zeros, so P = 0 multiplies zeros
+        const char *st = smem + stg * C::RING_STAGE + warp * C::BLK + half * 68;
+        // keys past the range were never loaded: zeros, so P = 0 multiplies zeros
+        auto stage_rows = [&](int r0) {
+            if (kr < n) {
+                dequant_2blocks(st + (r0 + kr) * tpitch, frow);
+            } else {
 #pragma unroll
-            for (int i = 0; i < 16; ++i) reinterpret_cast<uint4 *>(frow)[i] = make_uint4(0u, 0u, 0u, 0u);
-        }
-        __syncwarp();                                        // ring stage read, f16 tile complete
-        if (lane == 0) mbar_arrive(&empty[stg]);
-        decode_tile<D, C::FPITCH>(wk, wv, n, qa, cx, o, m_run, l_part, lane);
-        __syncwarp();                                        // f16 tile read before the next dequant
+                for (int i = 0; i < 8; ++i) reinterpret_cast<uint4 *>(frow)[i] = make_uint4(0u, 0u, 0u, 0u);
+            }
+            __syncwarp();
+        };
+        uint32_t pa[4];
+        stage_rows(0);                                       // K
+        decode_scores<D, C::FPITCH>(buf, n, qa, cx, o, m_run, l_part, lane, pa);
+        __syncwarp();                                        // K tile read before it is overwritten
+        stage_rows(C::KEYS);                                 // V
+        if (lane == 0) mbar_arrive(&empty[stg]);             // this warp is done with the ring stage
+        decode_pv<D, C::FPITCH>(buf, pa, o, lane);
+        __syncwarp();                                        // V tile read before the next stage's K
     }
     decode_store<D>(a, b, g, sp, o, m_run, l_part, lane);
 }
