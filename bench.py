@@ -38,6 +38,9 @@ sys.path.insert(0, os.path.join(ROOT, "voxtral.cpp_b200"))
 ENC = dict(n=1500, H=20, D=64, layers=32)
 DEC = dict(n_seq=256, Hq=32, Hkv=8, D=128, lo=512, hi=16384)
 METRIC_ENC = "attn TFLOP/s (prefill/encoder)"
+ENC_TRAFFIC_BYTES = 11_581_696          # one encoder launch, from the committed ncu capture
+DEC_TRAFFIC_RATIO_F16 = (1_058_088_000 + 7_246_080) / 1_057_517_568   # (read + write) / KV bytes, 32 streams
+DEC_TRAFFIC_RATIO_Q8 = (562_370_304 + 6_304_000) / 561_806_208
 METRIC_DEC = "KV GB/s (decode)"
 
 
@@ -219,7 +222,11 @@ def run_encoder(args, rank, world, local):
         "audio_sec_per_sec": round(30.0 * args.steps * world / (ms * 1e-3), 1),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     "traffic": None, "peak_src": f"{peaks['src']} bf16 dense (burst)",
+                     # dram__bytes_read + dram__bytes_write of one launch, ncu --set full capture
+                     # (profiles/fa_prefill_sm100_encoder_cfg2.md): 11.58 MB read (= Q+K+V), 0 written
+                     # (the 7.68 MB output stays in L2 during the launch)
+                     "traffic": ENC_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
+                     "peak_src": f"{peaks['src']} bf16 dense (burst)",
                      "per_launch_ms": round(launch_ms, 5),
                      "per_launch_flop": enc_flops_per_layer()},
         "e2e": e2e,
@@ -374,7 +381,11 @@ def run_decode(args, rank, world, local):
                    "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.1f} GB KV per step)",
                    "parallelism": f"dp{world} (independent streams per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "frac": round(achieved / peaks["hbm_gbs"], 4),
+                     # DRAM bytes per KV byte from the committed 32-stream ncu captures
+                     # (profiles/fa_decode_*_cfg5.md): reads = algorithmic KV bytes, + partials
+                     "traffic": round(kv_bytes * (DEC_TRAFFIC_RATIO_Q8 if q8 else DEC_TRAFFIC_RATIO_F16)),
+                     "traffic_unit": "bytes per step (scaled from the capture by KV bytes)",
                      "peak_src": f"{peaks['src']} copy bandwidth"},
         "gpu_launches": args.steps * 2,
         "clocks": clocks.summary(),
@@ -440,8 +451,11 @@ def main():
             import copy
             dargs = copy.copy(args)
             dargs.steps, dargs.warmup = 5, 3
-            d = run_decode(dargs, rank, world, local)
-            res["decode"] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "roofline", "config")}
+            for kv, key in (("f16", "decode"), ("q8_0", "decode_q8_0")):
+                dargs.kv = kv
+                d = run_decode(dargs, rank, world, local)
+                res[key] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "roofline", "config")}
+                torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
