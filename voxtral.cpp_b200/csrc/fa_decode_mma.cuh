@@ -205,6 +205,8 @@ template <int D>
 __global__ void __launch_bounds__(128, 2)
 fa_decode_mma_kernel(const SplitArgs a, int n_items)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     using C = DecodeCfg<D>;
     constexpr int KC = D / 16;                      // 16-wide chunks of the head dim
     extern __shared__ __align__(128) char smem[];

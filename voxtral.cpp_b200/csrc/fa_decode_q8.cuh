@@ -93,6 +93,8 @@ template <int D>
 __global__ void __launch_bounds__(DecodeQ8Cfg<D>::NTHREADS, 1)
 fa_decode_q8_kernel(const SplitArgs a, int hpc)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     using C = DecodeQ8Cfg<D>;
     constexpr int KC = D / 16, NB = D / 8;
     extern __shared__ __align__(128) char smem[];

@@ -233,6 +233,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
     }
+    grid_dep_wait();            // barriers, TMEM and the constant block above overlap the previous kernel
+    grid_dep_launch();
     if constexpr (C::ROWSUM) {
         // constant block [128 keys][64 columns] f16 in the V tiles' 128-byte
         // swizzled layout: column 0 is 1.0 (16-byte chunk 0 of key row k sits at

@@ -98,6 +98,8 @@ template <int D, int KVT, int MAXR>
 __global__ void __launch_bounds__(128)
 fa_splitkv_kernel(const SplitArgs a)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     using C = SplitCfg<D, KVT>;
     constexpr int TK = C::TK, PITCH = C::PITCH, STAGES = C::STAGES;
     constexpr int QP = D / 2 + 4;            // padded half-row of Q (floats)
@@ -427,6 +429,8 @@ template <int D, int MAXR>
 __global__ void __launch_bounds__(128)
 fa_combine_kernel(const SplitArgs a, int gy)
 {
+    grid_dep_wait();
+    grid_dep_launch();
     const int lane = threadIdx.x & 31;
     const long long row_id = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
     const int rows = a.tok_per_cta * a.hc;

@@ -19,6 +19,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <utility>
 
 #include "../../include/vtx_fa.h"
 #include "vtx_ptx.cuh"
@@ -226,6 +227,8 @@ PrefillPlan plan_prefill(const Geo &g, const vtx_tensor *q, const vtx_tensor *k,
 
 __global__ void convert_kv_f16_kernel(const char *src, long long nb1, long long nb2, long long nb3, int type,
                                       int D, int n_kv, int H, int Bk, __half *dst) {
+    grid_dep_wait();
+    grid_dep_launch();
     const long long total = (long long)Bk * H * n_kv * D;
     for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (long long)gridDim.x * blockDim.x) {
@@ -244,6 +247,24 @@ __global__ void convert_kv_f16_kernel(const char *src, long long nb1, long long 
         }
         dst[i] = __float2half_rn(x);
     }
+}
+
+// Every kernel is launched with programmatic stream serialisation (PDL): it
+// may be scheduled while the previous kernel on the stream drains, and waits
+// for it in-kernel (grid_dep_wait) before touching global memory.
+template <typename... KArgs, typename... Args>
+int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
 }
 
 int encode_kv_map(CUtensorMap *m, const void *ptr, int D, int n_kv, int H, int Bk, size_t nb1, size_t nb2,
@@ -306,12 +327,12 @@ int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
             return VTX_ERR_CUDA;
         attr_done[dev] = 1;
     }
-    fa_splitkv_kernel<D, KVT, MAXR><<<grid, 128, smem, st>>>(a);
-    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (launch_pdl(fa_splitkv_kernel<D, KVT, MAXR>, grid, dim3(128), smem, st, a) != VTX_OK) return VTX_ERR_CUDA;
     if (!a.write_final) {
         const long long rows = (long long)a.B * grid.y * a.n_qtiles * a.tok_per_cta * a.hc;
-        fa_combine_kernel<D, MAXR><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, (int)grid.y);
-        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+        if (launch_pdl(fa_combine_kernel<D, MAXR>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a,
+                       (int)grid.y) != VTX_OK)
+            return VTX_ERR_CUDA;
     }
     return VTX_OK;
 }
@@ -336,12 +357,14 @@ int launch_decode_mma_t(const SplitArgs &a, cudaStream_t st) {
         attr_done[dev] = 1;
     }
     const long long items = (long long)a.B * a.Hkv * a.n_splits;
-    fa_decode_mma_kernel<D><<<(unsigned)((items + C::WARPS - 1) / C::WARPS), 128, C::SMEM, st>>>(a, (int)items);
-    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (launch_pdl(fa_decode_mma_kernel<D>, dim3((unsigned)((items + C::WARPS - 1) / C::WARPS)), dim3(128), C::SMEM,
+                   st, a, (int)items) != VTX_OK)
+        return VTX_ERR_CUDA;
     if (!a.write_final) {
         const long long rows = (long long)a.B * a.Hkv * a.G;
-        fa_combine_kernel<D, 4><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, a.Hkv);
-        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+        if (launch_pdl(fa_combine_kernel<D, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
+            VTX_OK)
+            return VTX_ERR_CUDA;
     }
     return VTX_OK;
 }
@@ -377,12 +400,13 @@ int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
     }
     const long long items = (long long)a.B * (a.Hkv / hpc) * a.n_splits;
     if (items > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
-    fa_decode_q8_kernel<128><<<(unsigned)items, C::NTHREADS, C::SMEM, st>>>(a, hpc);
-    if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+    if (launch_pdl(fa_decode_q8_kernel<128>, dim3((unsigned)items), dim3(C::NTHREADS), C::SMEM, st, a, hpc) != VTX_OK)
+        return VTX_ERR_CUDA;
     if (!a.write_final) {
         const long long rows = (long long)a.B * a.Hkv * a.G;
-        fa_combine_kernel<128, 4><<<(unsigned)((rows + 3) / 4), 128, 0, st>>>(a, a.Hkv);
-        if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+        if (launch_pdl(fa_combine_kernel<128, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
+            VTX_OK)
+            return VTX_ERR_CUDA;
     }
     return VTX_OK;
 }
@@ -426,8 +450,7 @@ int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtenso
             return VTX_ERR_CUDA;
         attr_done[dev] = 1;
     }
-    fa_prefill_sm100_kernel<D, NQT, HM, UF><<<grid, C::NTHREADS, C::SMEM, st>>>(mk, mv, mo, a);
-    return cudaGetLastError() == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
+    return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo, a);
 }
 
 template <int D, int NQT>
@@ -522,11 +545,13 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
             __half *vc = reinterpret_cast<__half *>(static_cast<char *>(workspace) + pp.conv_bytes / 2);
             const long long total = (long long)g.Bkv * g.Hkv * g.n_kv * g.D;
             const int blocks = (int)std::min<long long>((total + 255) / 256, 8LL * ds->sms);
-            convert_kv_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const char *>(k->data), k->nb[1], k->nb[2],
-                                                          k->nb[3], k->type, g.D, g.n_kv, g.Hkv, g.Bkv, kc);
-            convert_kv_f16_kernel<<<blocks, 256, 0, st>>>(static_cast<const char *>(v->data), v->nb[1], v->nb[2],
-                                                          v->nb[3], v->type, g.D, g.n_kv, g.Hkv, g.Bkv, vc);
-            if (cudaGetLastError() != cudaSuccess) return VTX_ERR_CUDA;
+            if (launch_pdl(convert_kv_f16_kernel, dim3(blocks), dim3(256), 0, st, static_cast<const char *>(k->data),
+                           (long long)k->nb[1], (long long)k->nb[2], (long long)k->nb[3], (int)k->type, g.D, g.n_kv,
+                           g.Hkv, g.Bkv, kc) != VTX_OK ||
+                launch_pdl(convert_kv_f16_kernel, dim3(blocks), dim3(256), 0, st, static_cast<const char *>(v->data),
+                           (long long)v->nb[1], (long long)v->nb[2], (long long)v->nb[3], (int)v->type, g.D, g.n_kv,
+                           g.Hkv, g.Bkv, vc) != VTX_OK)
+                return VTX_ERR_CUDA;
             kp = kc;
             vp = vc;
             knb1 = vnb1 = (size_t)g.D * 2;

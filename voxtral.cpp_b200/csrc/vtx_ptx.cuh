@@ -66,6 +66,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t phase, int *er
     return false;
 }
 
+// ---- programmatic dependent launch --------------------------------------------
+// Every kernel of this library is launched with programmatic stream
+// serialisation, so it may be scheduled while the previous kernel on the
+// stream drains.  grid_dep_wait() blocks until that kernel has completed and
+// its memory is visible (it returns at once when there is none); every thread
+// calls it before touching global memory.  grid_dep_launch() lets the next
+// kernel be scheduled early; that kernel launches only once every CTA of this
+// grid has issued the call (i.e. is resident), so it cannot starve this grid.
+__device__ __forceinline__ void grid_dep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- fences -----------------------------------------------------------------
 __device__ __forceinline__ void fence_proxy_async_smem() {
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
