@@ -392,6 +392,110 @@ def run_decode(args, rank, world, local):
     }
 
 
+# ---- KV append (decoder cache update: RoPE + cache write) ---------------------------
+def run_kv_append(args, rank, world, local):
+    """vtx_kv_append on the decoder shape (GQA 32/8 x 128, RoPE base 1e6):
+    (1) bandwidth: 8192 tokens per call (a long prefill chunk) into an F16 or
+    Q8_0 cache, GB/s of algorithmic bytes (Q/K/V read, roped Q and cache rows
+    written) against the HBM copy peak; (2) latency: the 256-stream decode
+    step, one token per stream into its own cache (per-stream bases)."""
+    import numpy as np
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    q8 = getattr(args, "kv", "f16") == "q8_0"
+    kvt = vtx_attn.Q8_0 if q8 else vtx_attn.F16
+    Hq, Hkv, D = DEC["Hq"], DEC["Hkv"], DEC["D"]
+    hb = D // 32 * 34 if q8 else D * 2
+    g = torch.Generator(device=dev)
+    g.manual_seed(91 + rank)
+    T = 8192
+    q = torch.randn((T, Hq, D), generator=g, device=dev)
+    k = torch.randn((T, Hkv, D), generator=g, device=dev)
+    v = torch.randn((T, Hkv, D), generator=g, device=dev)
+    pos = torch.arange(T, dtype=torch.int32, device=dev) + 391
+    slots = torch.arange(T, dtype=torch.int32, device=dev)
+    kc = torch.empty((T, Hkv * hb), dtype=torch.uint8, device=dev)
+    vc = torch.empty_like(kc)
+    qo = torch.empty_like(q)
+    stream = torch.cuda.Stream(device=dev)
+
+    def call():
+        vtx_attn.kv_append(k, v, pos, slots, kc, vc, kvt, 1e6, q=q, q_out=qo, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        e0.record(stream)
+        for _ in range(args.steps):
+            call()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+    ms_local = e0.elapsed_time(e1) / args.steps
+    ms = barrier_max(ms_local, world)
+    nbytes = T * ((Hq + 2 * Hkv) * D * 4 + Hq * D * 4 + 2 * Hkv * hb)
+    peaks = load_peaks()
+    achieved = nbytes / (ms_local * 1e-3) / 1e9
+
+    # 256-stream decode step: one token per stream, each into its own cache
+    S = DEC["n_seq"]
+    W = 8192
+    caches_k = torch.empty((S, W, Hkv * hb), dtype=torch.uint8, device=dev)
+    caches_v = torch.empty_like(caches_k)
+    kp = torch.tensor([caches_k[i].data_ptr() for i in range(S)], dtype=torch.int64, device=dev)
+    vp = torch.tensor([caches_v[i].data_ptr() for i in range(S)], dtype=torch.int64, device=dev)
+    rng = np.random.default_rng(4321 + rank)
+    lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S)
+    spos = torch.from_numpy(lens.astype(np.int32)).to(dev)
+    sslot = torch.from_numpy((lens % W).astype(np.int32)).to(dev)
+    sq, sk, sv = q[:S], k[:S], v[:S]
+    sqo = torch.empty_like(sq)
+
+    def step():
+        vtx_attn.kv_append(sk, sv, spos, sslot, None, None, kvt, 1e6, q=sq, q_out=sqo, k_cache_ptrs=kp,
+                           v_cache_ptrs=vp, cache_nb1=Hkv * hb, stream=stream)
+
+    with torch.cuda.stream(stream):
+        for _ in range(max(3, args.warmup)):
+            step()
+    torch.cuda.synchronize()
+    # graph-captured so the host's per-call cost does not enter the device time
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for _ in range(10):
+            step()
+    torch.cuda.synchronize()
+    with torch.cuda.stream(stream):
+        graph.replay()
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    step_us = e0.elapsed_time(e1) / (args.steps * 10) * 1e3
+    return {
+        "metric": "KV append GB/s (decoder cache update)", "value": round(nbytes * world / (ms * 1e-3) / 1e9, 1),
+        "unit": "GB/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q8_0" if q8 else "f16", "data": "synthetic N(0,1) f32 Q/K/V, seeded per rank",
+        "config": {"workload": f"decoder KV append: {T} tokens x GQA 32/8 x 128, RoPE base 1e6, "
+                               f"{'Q8_0' if q8 else 'f16'} cache rows; plus the {S}-stream decode step",
+                   "parallelism": f"dp{world}"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / peaks["hbm_gbs"], 4), "traffic": None,
+                     "per_call_bytes": int(nbytes)},
+        "decode_step_us": round(step_us, 2),
+        "gpu_launches": args.steps * 11,
+        "clocks": clocks.summary(),
+    }
+
+
 # ---- reference arm ------------------------------------------------------------------
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -425,7 +529,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode", "kv_append"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
@@ -459,7 +563,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
-        res = run_decode(args, rank, world, local)
+        res = run_decode(args, rank, world, local) if args.workload == "decode" else \
+            run_kv_append(args, rank, world, local)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

@@ -179,6 +179,43 @@ VTX_API size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *b
 #define VTX_NOALLOC_SCRATCH_BYTES (32u << 20)
 VTX_API int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *batch, void *stream);
 
+/* Decoder KV-cache update: RoPE of Q and K, then the K/V cache write, in one
+ * pass.  Replaces per decoder layer the ggml_rope_ext of Q and K (mode 0,
+ * freq_base = dec_rope_theta, freq_scale 1, no YaRN) and the ggml_cpy of K
+ * and V into the cache rows at kv_offset (src/voxtral.cpp:1744-1770), and the
+ * shift-left memmove of the full cache window (src/voxtral.cpp:1237-1266).
+ * - Token t of q / k / v is a row of heads x head_dim F32 values (heads
+ *   contiguous, token stride *_nb1 bytes).  It is rotated with positions[t].
+ * - K and V go to cache row slots[t] (a ring slot).  With
+ *   slots[t] = (tokens so far + t) % window the cache holds the same rows as
+ *   the reference after its shift-left, and decode attention does not depend
+ *   on their order.  Prefill writes rows 0..n-1 in order.
+ * - A cache row is ggml's [kv_dim] row: n_head_kv heads of head_dim values in
+ *   the cache type (F32, F16, or Q8_0 blocks of 34 bytes).  Row r is at
+ *   k_cache + r * cache_nb1, or at k_cache_ptrs[t] + r * cache_nb1 when the
+ *   per-token base array is given (one cache per stream in batched decode).
+ * - q_out receives the rotated Q (it may equal q); with q_out NULL only K
+ *   and V are processed.
+ * positions, slots and the pointer arrays are device memory.  Asynchronous
+ * on `stream`; no allocation. */
+typedef struct {
+    int32_t n_tokens, n_head_q, n_head_kv, head_dim;
+    int32_t kv_type;                    /* VTX_TYPE_F32 / VTX_TYPE_F16 / VTX_TYPE_Q8_0 */
+    float freq_base;                    /* RoPE base (voxtral.cpp: 1e6) */
+    const float *q; size_t q_nb1;
+    float *q_out; size_t q_out_nb1;
+    const float *k; size_t k_nb1;
+    const float *v; size_t v_nb1;
+    const int32_t *positions;
+    const int32_t *slots;
+    void *k_cache, *v_cache;
+    const void *const *k_cache_ptrs;    /* optional, [n_tokens] */
+    const void *const *v_cache_ptrs;
+    size_t cache_nb1;
+    int32_t reserved[4];
+} vtx_kv_append_args;
+VTX_API int vtx_kv_append(const vtx_kv_append_args *args, void *stream);
+
 /* Diagnostic: synchronises `stream`, returns and clears the device-side error
  * word of the current device (0 = none).  Kernels set it instead of hanging
  * when a bounded pipeline wait runs out, or when a batched-decode stream base

@@ -81,6 +81,9 @@ def lib():
         L.vtx_ref_flash_attn_ext.restype = ctypes.c_int
         L.vtx_ref_decode_batched.argtypes = [ctypes.POINTER(DecodeBatch), ctypes.c_int, ctypes.c_int]
         L.vtx_ref_decode_batched.restype = ctypes.c_int
+        L.vtx_ref_kv_append.argtypes = [ctypes.c_int] * 5 + [ctypes.c_float] + [vp] * 8 + [ctypes.c_size_t,
+                                                                                          ctypes.c_int]
+        L.vtx_ref_kv_append.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -203,6 +206,40 @@ def decode_batched(q: np.ndarray, k_list, v_list, kv_len, scale: float, kv_type:
     if rc != 0:
         raise ValueError(f"oracle rejected batch: status {rc}")
     return dst
+
+
+def cache_head_bytes(kv_type: int, D: int) -> int:
+    return D * 4 if kv_type == F32 else D * 2 if kv_type == F16 else D // QK8_0 * Q8_0_BLOCK
+
+
+def kv_append(q: np.ndarray | None, k: np.ndarray, v: np.ndarray, positions, slots, kv_type: int,
+              freq_base: float, k_cache: np.ndarray, v_cache: np.ndarray, mode: int = MODE_GGML):
+    """Decoder KV update on the host: RoPE of Q and K (ggml mode 0) and the
+    K/V cache write at rows ``slots`` (uint8 caches [n_rows, Hkv * head bytes],
+    written in place).  q: (T, Hq, D) or None, k/v: (T, Hkv, D) float32.
+    Returns the roped Q (or None)."""
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    T, Hkv, D = k.shape
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    sl = np.ascontiguousarray(slots, dtype=np.int32)
+    assert k_cache.flags.c_contiguous and v_cache.flags.c_contiguous and k_cache.dtype == np.uint8
+    assert k_cache.shape[1] == Hkv * cache_head_bytes(kv_type, D) and v_cache.shape == k_cache.shape
+    assert sl.max(initial=-1) < k_cache.shape[0] and sl.min(initial=0) >= 0
+    qo = None
+    qp = qop = None
+    Hq = 0
+    if q is not None:
+        q = np.ascontiguousarray(q, dtype=np.float32)
+        Hq = q.shape[1]
+        qo = np.empty_like(q)
+        qp, qop = q.ctypes.data, qo.ctypes.data
+    rc = lib().vtx_ref_kv_append(T, Hq, Hkv, D, kv_type, freq_base, qp, qop, k.ctypes.data, v.ctypes.data,
+                                 pos.ctypes.data, sl.ctypes.data, k_cache.ctypes.data, v_cache.ctypes.data,
+                                 k_cache.strides[0], mode)
+    if rc != 0:
+        raise ValueError(f"oracle rejected kv_append: status {rc}")
+    return qo
 
 
 # ---- reference masks (host-built, exactly as voxtral.cpp fills them) ------

@@ -440,3 +440,78 @@ int vtx_ref_decode_batched(const vtx_decode_batch *b, int mode, int n_threads)
     }
     return 0;
 }
+
+/* ---- KV append: RoPE + cache write (decoder layer) -------------------------
+ * Restates the decoder layer's cache update (src/voxtral.cpp:1744-1770):
+ *   q = ggml_rope_ext(q, positions, NULL, head_dim, mode 0, n_ctx_orig 0,
+ *                     freq_base, freq_scale 1, ext_factor 0, attn_factor 1,
+ *                     beta_fast 0, beta_slow 0);   k = the same;
+ *   ggml_cpy(k -> K cache row kv_offset + i), ggml_cpy(v -> V cache row).
+ * ggml's CPU rope for mode 0 ("normal": adjacent pairs (x[2i], x[2i+1])) as
+ * published (ggml_rope_cache_init / rope_yarn in ggml-cpu/ops.cpp): one float
+ * theta per token, starting at (float)pos and multiplied by
+ * theta_scale = powf(freq_base, -2/n_dims) after each pair; per pair
+ * c = cosf(theta), s = sinf(theta); y0 = x0*c - x1*s, y1 = x0*s + x1*c.
+ * The cache write converts each float row to the cache type: F32 unchanged,
+ * F16 round-to-nearest-even, Q8_0 with the CPU from_float (quantize_q8_0_rne).
+ * slots[i] is the cache row of token i; the build replaces the reference's
+ * shift-left memmove (src/voxtral.cpp:1237-1266) by a ring slot, which keeps
+ * the same set of rows.
+ * Mode VTX_REF_FP64: theta_i = pos * freq_base^(-2i/n_dims) and cos/sin in
+ * double (an independent truth for the rotation; cache writes as above).
+ * q, k, v, q_out are contiguous [n_tokens][n_head][head_dim] floats. */
+static void rope_row(const float *x, float *y, int D, int32_t pos, float theta_scale, double freq_base, int mode)
+{
+    float theta = (float)pos;
+    for (int i = 0; i < D / 2; i++) {
+        float c, s;
+        if (mode == VTX_REF_FP64) {
+            const double th = (double)pos * pow(freq_base, -2.0 * i / D);
+            c = (float)cos(th);
+            s = (float)sin(th);
+        } else {
+            c = cosf(theta);
+            s = sinf(theta);
+            theta *= theta_scale;
+        }
+        const float x0 = x[2 * i], x1 = x[2 * i + 1];
+        y[2 * i] = x0 * c - x1 * s;
+        y[2 * i + 1] = x0 * s + x1 * c;
+    }
+}
+
+static void cache_store(const float *x, void *dst, int D, int kv_type)
+{
+    if (kv_type == VTX_TYPE_F32) memcpy(dst, x, (size_t)D * 4);
+    else if (kv_type == VTX_TYPE_F16) vtx_ref_f32_to_f16(x, (uint16_t *)dst, D);
+    else vtx_ref_quantize_q8_0_rne(x, (vtx_block_q8_0 *)dst, D);
+}
+
+int vtx_ref_kv_append(int n_tokens, int n_head_q, int n_head_kv, int head_dim, int kv_type, float freq_base,
+                      const float *q, float *q_out, const float *k, const float *v, const int32_t *positions,
+                      const int32_t *slots, void *k_cache, void *v_cache, size_t cache_nb1, int mode)
+{
+    if (!k || !v || !positions || !slots || !k_cache || !v_cache) return VTX_ERR_NULL;
+    if (head_dim % 32 || head_dim <= 0) return VTX_ERR_UNSUPPORTED;
+    const int D = head_dim;
+    const float theta_scale = powf(freq_base, -2.0f / (float)D);
+    const size_t head_bytes = kv_type == VTX_TYPE_F32 ? (size_t)D * 4
+                            : kv_type == VTX_TYPE_F16 ? (size_t)D * 2 : (size_t)D / 32 * sizeof(vtx_block_q8_0);
+    float *tmp = (float *)malloc((size_t)D * sizeof(float));
+    if (!tmp) return VTX_ERR_CUDA;
+    for (int t = 0; t < n_tokens; t++) {
+        if (q && q_out)
+            for (int h = 0; h < n_head_q; h++)
+                rope_row(q + ((size_t)t * n_head_q + h) * D, q_out + ((size_t)t * n_head_q + h) * D, D,
+                         positions[t], theta_scale, freq_base, mode);
+        char *krow = (char *)k_cache + (size_t)slots[t] * cache_nb1;
+        char *vrow = (char *)v_cache + (size_t)slots[t] * cache_nb1;
+        for (int h = 0; h < n_head_kv; h++) {
+            rope_row(k + ((size_t)t * n_head_kv + h) * D, tmp, D, positions[t], theta_scale, freq_base, mode);
+            cache_store(tmp, krow + h * head_bytes, D, kv_type);
+            cache_store(v + ((size_t)t * n_head_kv + h) * D, vrow + h * head_bytes, D, kv_type);
+        }
+    }
+    free(tmp);
+    return 0;
+}

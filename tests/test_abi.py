@@ -29,7 +29,7 @@ def test_header_declares_the_entry_points():
     syms = set(declared_symbols())
     assert {"vtx_flash_attn_ext", "vtx_flash_attn_ext_workspace", "vtx_flash_attn_decode_batched",
             "vtx_flash_attn_decode_batched_workspace", "vtx_strerror", "vtx_abi_version",
-            "vtx_read_device_error"} <= syms
+            "vtx_read_device_error", "vtx_flash_attn_decode_batched_noalloc", "vtx_kv_append"} <= syms
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -54,6 +54,47 @@ def test_struct_layouts_match_ctypes(tmp_path):
     assert vals == [ctypes.sizeof(vtx_attn.VtxTensor), ctypes.sizeof(vtx_attn.FaParams),
                     ctypes.sizeof(vtx_attn.DecodeBatch), vtx_attn.VtxTensor.data.offset,
                     vtx_attn.DecodeBatch.q.offset, 34]
+
+
+def test_kv_append_args_layout(tmp_path):
+    import vtx_attn
+    src = tmp_path / "probe_kv.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vtx_fa.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu\\n", sizeof(vtx_kv_append_args),'
+                   ' offsetof(vtx_kv_append_args, q), offsetof(vtx_kv_append_args, positions),'
+                   ' offsetof(vtx_kv_append_args, k_cache_ptrs), offsetof(vtx_kv_append_args, cache_nb1));'
+                   ' return 0;}\n')
+    exe = tmp_path / "probe_kv"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    K = vtx_attn.KvAppendArgs
+    assert vals == [ctypes.sizeof(K), K.q.offset, K.positions.offset, K.k_cache_ptrs.offset, K.cache_nb1.offset]
+
+
+def test_kv_append_validation_without_device(lib):
+    """vtx_kv_append rejects bad arguments with status codes before any device work."""
+    import vtx_attn as V
+    B = ctypes.byref
+
+    def args(**kw):
+        a = V.KvAppendArgs()
+        a.n_tokens, a.n_head_q, a.n_head_kv, a.head_dim, a.kv_type, a.freq_base = 4, 32, 8, 128, V.F16, 1e6
+        a.k, a.v, a.positions, a.slots = 0x1000, 0x2000, 0x3000, 0x4000
+        a.k_nb1 = a.v_nb1 = 8 * 128 * 4
+        a.k_cache, a.v_cache, a.cache_nb1 = 0x10000, 0x20000, 8 * 128 * 2
+        for key, val in kw.items():
+            setattr(a, key, val)
+        return a
+
+    assert lib.vtx_kv_append(None, None) == -1
+    assert lib.vtx_kv_append(B(args(n_tokens=0)), None) == 0          # nothing to do, no device needed
+    assert lib.vtx_kv_append(B(args(k=None)), None) == -1
+    assert lib.vtx_kv_append(B(args(kv_type=30)), None) == -2
+    assert lib.vtx_kv_append(B(args(head_dim=96)), None) == -5
+    assert lib.vtx_kv_append(B(args(n_head_kv=0)), None) == -3
+    assert lib.vtx_kv_append(B(args(k_nb1=8 * 128 * 4 + 4)), None) == -4    # rows not 8-byte aligned
+    assert lib.vtx_kv_append(B(args(cache_nb1=8 * 128 * 2 + 2)), None) == -4  # F16 cache rows not 4-byte aligned
+    assert lib.vtx_kv_append(B(args(q_out=0x5000)), None) == -1         # q_out without q
 
 
 def test_abi_version_and_strerror(lib):

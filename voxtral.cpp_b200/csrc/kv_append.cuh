@@ -1,0 +1,130 @@
+// kv_append.cuh — decoder KV-cache update for sm_100a: RoPE of Q and K and the
+// K/V cache write, fused into one HBM-bound pass.
+//
+// Replaces, per decoder layer, the two ggml_rope_ext nodes, the ggml_cont and
+// the two ggml_cpy nodes of src/voxtral.cpp:1744-1770, and the shift-left
+// memmove of the cache window (src/voxtral.cpp:1237-1266): each token's rows
+// go to a caller-chosen cache row (a ring slot), and decode attention over the
+// cache is invariant to the order of its rows.
+//
+// RoPE follows ggml's mode 0 ("normal": adjacent pairs (x[2i], x[2i+1])) with
+// freq_scale 1, ext_factor 0, attn_factor 1, as voxtral.cpp calls it.  Like
+// ggml's CPU rope cache, the angle of pair i is the float recurrence
+// theta_0 = (float)pos, theta_{i+1} = theta_i * theta_scale with
+// theta_scale = powf(freq_base, -2/head_dim) computed on the host, so the
+// angles are the same floats ggml uses; cos/sin are taken in double and
+// rounded to float (the correctly rounded values).
+//
+// One CTA per token builds its cos/sin table once; a warp streams one row
+// (tensor, head) at a time, a lane owning head_dim/32 consecutive elements.
+// Cache types: F32 (the reference's own cache), F16 (round to nearest even)
+// and Q8_0 (per 32 values d = amax/127 stored as f16,
+// q = round-half-even(x * 127/amax), as ggml's CPU from_float; a block is
+// 32/E lanes, amax by shuffles).
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+#include "vtx_ptx.cuh"
+
+namespace vtx {
+
+struct KvAppendArgs {
+    int T, Hq, Hkv, kv_type;
+    float theta_scale;
+    const float *q; long long q_nb1;        // token stride (floats); heads contiguous
+    const float *k; long long k_nb1;
+    const float *v; long long v_nb1;
+    float *q_out; long long qo_nb1;
+    const int *positions, *slots;
+    char *k_cache, *v_cache;
+    const void *const *k_ptrs; const void *const *v_ptrs;   // optional per-token cache bases
+    long long cache_nb1;                    // bytes per cache row
+};
+
+// One CTA per token: threads 0..D/2-1 build the token's cos/sin table in
+// shared memory (thread i runs the float angle recurrence i steps, then one
+// double-precision sincos rounded to float), then 8 warps stream the token's
+// Hq + 2 Hkv rows, one row per warp at a time.
+template <int D>
+__global__ void __launch_bounds__(256)
+kv_append_kernel(const KvAppendArgs a)
+{
+    grid_dep_wait();
+    grid_dep_launch();
+    constexpr int E = D / 32;                               // elements per lane
+    __shared__ float2 cs[D / 2];                            // (cos, sin) of pair i
+    const int t = blockIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x < D / 2) {
+        float theta = (float)a.positions[t];
+        for (int i = 0; i < (int)threadIdx.x; ++i) theta *= a.theta_scale;
+        double sd, cd;
+        sincos((double)theta, &sd, &cd);
+        cs[threadIdx.x] = make_float2((float)cd, (float)sd);
+    }
+    __syncthreads();
+    const int slot = a.slots[t];
+    const int per_tok = a.Hq + 2 * a.Hkv;
+    for (int r = warp; r < per_tok; r += blockDim.x >> 5) {
+        const int kind = r < a.Hq ? 0 : (r < a.Hq + a.Hkv ? 1 : 2);   // Q, K, V
+        const int h = kind == 0 ? r : (kind == 1 ? r - a.Hq : r - a.Hq - a.Hkv);
+        const float *src = kind == 0 ? a.q + (long long)t * a.q_nb1
+                                     : (kind == 1 ? a.k + (long long)t * a.k_nb1 : a.v + (long long)t * a.v_nb1);
+        src += (long long)h * D + lane * E;
+        float x[E];
+#pragma unroll
+        for (int i = 0; i < E; i += 2) {
+            const float2 p = *reinterpret_cast<const float2 *>(src + i);
+            x[i] = p.x;
+            x[i + 1] = p.y;
+        }
+        if (kind != 2) {
+#pragma unroll
+            for (int j = 0; j < E / 2; ++j) {
+                const float2 c = cs[lane * E / 2 + j];
+                const float x0 = x[2 * j], x1 = x[2 * j + 1];
+                x[2 * j] = x0 * c.x - x1 * c.y;
+                x[2 * j + 1] = x0 * c.y + x1 * c.x;
+            }
+        }
+        if (kind == 0) {
+            float *dst = a.q_out + (long long)t * a.qo_nb1 + (long long)h * D + lane * E;
+#pragma unroll
+            for (int i = 0; i < E; i += 2) *reinterpret_cast<float2 *>(dst + i) = make_float2(x[i], x[i + 1]);
+            continue;
+        }
+        char *base = kind == 1 ? (a.k_ptrs ? (char *)a.k_ptrs[t] : a.k_cache)
+                               : (a.v_ptrs ? (char *)a.v_ptrs[t] : a.v_cache);
+        char *crow = base + (long long)slot * a.cache_nb1;
+        if (a.kv_type == 0) {                               // F32
+            float *dst = reinterpret_cast<float *>(crow) + (long long)h * D + lane * E;
+#pragma unroll
+            for (int i = 0; i < E; i += 2) *reinterpret_cast<float2 *>(dst + i) = make_float2(x[i], x[i + 1]);
+        } else if (a.kv_type == 1) {                        // F16
+            __half *dst = reinterpret_cast<__half *>(crow) + (long long)h * D + lane * E;
+#pragma unroll
+            for (int i = 0; i < E; i += 2)
+                *reinterpret_cast<__half2 *>(dst + i) = __floats2half2_rn(x[i], x[i + 1]);
+        } else {                                            // Q8_0: 32 / E lanes per block
+            constexpr int LPB = 32 / E;
+            float amax = 0.f;
+#pragma unroll
+            for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+            for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+            const float id = amax != 0.f ? 127.f / amax : 0.f;
+            char *blk = crow + (long long)h * (D / 32) * 34 + (lane / LPB) * 34;
+            if (lane % LPB == 0) *reinterpret_cast<__half *>(blk) = __float2half_rn(amax / 127.f);
+            // the block's values start 2 bytes in: 2-byte stores stay aligned
+            unsigned short *qs = reinterpret_cast<unsigned short *>(blk + 2 + (lane % LPB) * E);
+#pragma unroll
+            for (int i = 0; i < E; i += 2) {
+                const uint32_t q0 = (uint32_t)(__float2int_rn(x[i] * id) & 0xff);
+                const uint32_t q1 = (uint32_t)(__float2int_rn(x[i + 1] * id) & 0xff);
+                qs[i / 2] = (unsigned short)(q0 | (q1 << 8));
+            }
+        }
+    }
+}
+
+}  // namespace vtx

@@ -27,6 +27,7 @@
 #include "fa_prefill_sm100.cuh"
 #include "fa_decode_mma.cuh"
 #include "fa_decode_q8.cuh"
+#include "kv_append.cuh"
 
 using namespace vtx;
 
@@ -709,6 +710,44 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
         return launch_decode_q8(a, hpc, static_cast<cudaStream_t>(stream));
     dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
     return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
+}
+
+int vtx_kv_append(const vtx_kv_append_args *p, void *stream) {
+    if (!p) return VTX_ERR_NULL;
+    if (p->n_tokens < 0 || p->n_head_kv <= 0 || p->n_head_q < 0) return VTX_ERR_SHAPE;
+    if (p->head_dim != 64 && p->head_dim != 128) return VTX_ERR_UNSUPPORTED;
+    if (p->kv_type != VTX_TYPE_F32 && p->kv_type != VTX_TYPE_F16 && p->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    if (p->n_tokens == 0) return VTX_OK;
+    if (!p->k || !p->v || !p->positions || !p->slots) return VTX_ERR_NULL;
+    if ((!p->k_cache && !p->k_cache_ptrs) || (!p->v_cache && !p->v_cache_ptrs)) return VTX_ERR_NULL;
+    if (p->q_out && (!p->q || p->n_head_q <= 0)) return VTX_ERR_NULL;
+    if (!(p->freq_base > 0.0f)) return VTX_ERR_SHAPE;
+    // float2 row loads / stores; half2 (F16) or 2-byte (Q8_0) cache stores
+    const uintptr_t rows = reinterpret_cast<uintptr_t>(p->k) | reinterpret_cast<uintptr_t>(p->v) | p->k_nb1 |
+                           p->v_nb1 | (p->q_out ? reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->q_out) |
+                                                      p->q_nb1 | p->q_out_nb1
+                                                : 0);
+    const uintptr_t cache = reinterpret_cast<uintptr_t>(p->k_cache) | reinterpret_cast<uintptr_t>(p->v_cache) |
+                            p->cache_nb1;
+    const unsigned calign = p->kv_type == VTX_TYPE_F32 ? 8 : p->kv_type == VTX_TYPE_F16 ? 4 : 2;
+    if (rows % 8 || cache % calign) return VTX_ERR_STRIDE;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    KvAppendArgs a{};
+    a.T = p->n_tokens; a.Hq = p->q_out ? p->n_head_q : 0; a.Hkv = p->n_head_kv; a.kv_type = p->kv_type;
+    a.theta_scale = std::pow(p->freq_base, -2.0f / (float)p->head_dim);   // as ggml: powf on the host
+    a.q = p->q; a.q_nb1 = (long long)(p->q_nb1 / 4);
+    a.q_out = p->q_out; a.qo_nb1 = (long long)(p->q_out_nb1 / 4);
+    a.k = p->k; a.k_nb1 = (long long)(p->k_nb1 / 4);
+    a.v = p->v; a.v_nb1 = (long long)(p->v_nb1 / 4);
+    a.positions = p->positions; a.slots = p->slots;
+    a.k_cache = static_cast<char *>(p->k_cache); a.v_cache = static_cast<char *>(p->v_cache);
+    a.k_ptrs = p->k_cache_ptrs; a.v_ptrs = p->v_cache_ptrs;
+    a.cache_nb1 = (long long)p->cache_nb1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return p->head_dim == 64 ? launch_pdl(kv_append_kernel<64>, dim3((unsigned)a.T), dim3(256), 0, st, a)
+                             : launch_pdl(kv_append_kernel<128>, dim3((unsigned)a.T), dim3(256), 0, st, a);
 }
 
 int vtx_read_device_error(void *stream) {

@@ -56,6 +56,21 @@ class DecodeBatch(ctypes.Structure):
                 ("reserved", ctypes.c_int32)]
 
 
+class KvAppendArgs(ctypes.Structure):
+    """vtx_kv_append_args (include/vtx_fa.h)."""
+    _fields_ = [("n_tokens", ctypes.c_int32), ("n_head_q", ctypes.c_int32),
+                ("n_head_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("kv_type", ctypes.c_int32), ("freq_base", ctypes.c_float),
+                ("q", ctypes.c_void_p), ("q_nb1", ctypes.c_size_t),
+                ("q_out", ctypes.c_void_p), ("q_out_nb1", ctypes.c_size_t),
+                ("k", ctypes.c_void_p), ("k_nb1", ctypes.c_size_t),
+                ("v", ctypes.c_void_p), ("v_nb1", ctypes.c_size_t),
+                ("positions", ctypes.c_void_p), ("slots", ctypes.c_void_p),
+                ("k_cache", ctypes.c_void_p), ("v_cache", ctypes.c_void_p),
+                ("k_cache_ptrs", ctypes.c_void_p), ("v_cache_ptrs", ctypes.c_void_p),
+                ("cache_nb1", ctypes.c_size_t), ("reserved", ctypes.c_int32 * 4)]
+
+
 _lib = None
 
 
@@ -85,6 +100,8 @@ def load(path: str = LIB_PATH):
     L.vtx_strerror.restype = ctypes.c_char_p
     L.vtx_abi_version.argtypes = []
     L.vtx_abi_version.restype = ctypes.c_int
+    L.vtx_kv_append.argtypes = [P(KvAppendArgs), ctypes.c_void_p]
+    L.vtx_kv_append.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -222,6 +239,43 @@ class DecodeBatchPlan:
                                                   self.workspace.numel(), ctypes.c_void_p(s.cuda_stream))
         _check(rc, "vtx_flash_attn_decode_batched")
         return out
+
+
+def kv_append(k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
+              k_cache: torch.Tensor, v_cache: torch.Tensor, kv_type: int, freq_base: float = 1e6, *,
+              q: Optional[torch.Tensor] = None, q_out: Optional[torch.Tensor] = None,
+              k_cache_ptrs: Optional[torch.Tensor] = None, v_cache_ptrs: Optional[torch.Tensor] = None,
+              cache_nb1: Optional[int] = None, stream: Optional[torch.cuda.Stream] = None) -> Optional[torch.Tensor]:
+    """vtx_kv_append: RoPE (ggml mode 0) of q and k, then k/v written into the
+    cache rows ``slots`` (F32, F16 or Q8_0 bytes).  k, v: (T, Hkv, D) float32
+    (heads contiguous), q: (T, Hq, D) float32 or None.  Caches: rows of
+    Hkv * head bytes, ``cache_nb1`` bytes apart (default: the row size).
+    Returns q_out (allocated when q is given and q_out is None)."""
+    T, Hkv, D = k.shape
+    for t in (k, v) + ((q,) if q is not None else ()):
+        if t.dtype != torch.float32 or t.stride(2) != 1 or t.stride(1) != D:
+            raise VtxError(-4, "q/k/v must be float32 with heads contiguous")
+    if q is not None and q_out is None:
+        q_out = torch.empty_like(q)
+    a = KvAppendArgs()
+    a.n_tokens, a.n_head_kv, a.head_dim, a.kv_type, a.freq_base = T, Hkv, D, kv_type, freq_base
+    if q is not None:
+        a.n_head_q, a.q, a.q_nb1 = q.shape[1], q.data_ptr(), q.stride(0) * 4
+        a.q_out, a.q_out_nb1 = q_out.data_ptr(), q_out.stride(0) * 4
+    a.k, a.k_nb1, a.v, a.v_nb1 = k.data_ptr(), k.stride(0) * 4, v.data_ptr(), v.stride(0) * 4
+    pos = positions.to(torch.int32).contiguous()
+    sl = slots.to(torch.int32).contiguous()
+    a.positions, a.slots = pos.data_ptr(), sl.data_ptr()
+    a.k_cache = k_cache.data_ptr() if k_cache is not None else None
+    a.v_cache = v_cache.data_ptr() if v_cache is not None else None
+    a.k_cache_ptrs = k_cache_ptrs.data_ptr() if k_cache_ptrs is not None else None
+    a.v_cache_ptrs = v_cache_ptrs.data_ptr() if v_cache_ptrs is not None else None
+    if cache_nb1 is None:
+        cache_nb1 = k_cache.stride(0) * k_cache.element_size()
+    a.cache_nb1 = cache_nb1
+    s = stream if stream is not None else torch.cuda.current_stream(k.device)
+    _check(load().vtx_kv_append(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "vtx_kv_append")
+    return q_out
 
 
 def read_device_error(stream: Optional[torch.cuda.Stream] = None) -> int:
