@@ -496,6 +496,69 @@ def run_kv_append(args, rank, world, local):
     }
 
 
+# ---- graph-replayed decode step (configs[2] and configs[3] decoders) --------------
+def run_decode_step(args, rank, world, local):
+    """The attention part of one decoded token for every layer (KV append +
+    decode attention per layer, device counters advanced), replayed from a
+    CUDA graph (decode_step.DecodeStepGraph), one stream (batch 1):
+      configs[2]: 30 layers, f16 cache, 391-token prefix, 200 steps;
+      26 layers, Q8_0 cache, 7300-token prefix (window 8192), 200 steps.
+    value = us per decoded token (graph); eager = the same calls from the host."""
+    import numpy as np
+    import torch
+    import vtx_attn
+    from decode_step import DecodeStepGraph
+
+    dev = torch.device("cuda", local)
+    res = {}
+    for name, L, kvt, start in (("configs[2]", 30, vtx_attn.F16, 391), ("configs[3]", 26, vtx_attn.Q8_0, 7300)):
+        g = DecodeStepGraph(L, 1, DEC["Hq"], DEC["Hkv"], DEC["D"], kvt, 8192, [start], device=dev)
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(61 + rank)
+        for l in range(L):                                   # prefill rows
+            k = torch.randn((start, DEC["Hkv"], DEC["D"]), generator=gen, device=dev)
+            g.fill(l, 0, k, torch.randn_like(k), torch.arange(start, dtype=torch.int32))
+        g.q.normal_(generator=gen)
+        g.k.normal_(generator=gen)
+        g.v.normal_(generator=gen)
+        g.step()                                             # eager first step + capture
+        for _ in range(max(3, args.warmup)):
+            g.step()
+        torch.cuda.synchronize()
+        n = 200
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(g.stream)
+        for _ in range(n):
+            g.step()
+        e1.record(g.stream)
+        torch.cuda.synchronize()
+        us = e0.elapsed_time(e1) / n * 1e3
+        e0.record(g.stream)
+        for _ in range(20):
+            g.step_eager()
+        e1.record(g.stream)
+        torch.cuda.synchronize()
+        us_eager = e0.elapsed_time(e1) / 20 * 1e3
+        kv = int(g.kv_len.item())
+        row = g.row
+        step_bytes = L * kv * row * 2
+        res[name] = {"layers": L, "kv_type": "q8_0" if kvt == vtx_attn.Q8_0 else "f16", "kv_len_at_end": kv,
+                     "us_per_token_graph": round(us, 1), "us_per_token_eager": round(us_eager, 1),
+                     "us_per_layer_graph": round(us / L, 2), "kv_GBps_graph": round(step_bytes / (us * 1e-6) / 1e9, 1)}
+        del g
+        torch.cuda.empty_cache()
+    peaks = load_peaks()
+    main = res["configs[2]"]
+    return {"metric": "decode step us/token (attention part, graph replay)", "value": main["us_per_token_graph"],
+            "unit": "us", "n_gpus": world, "steps": 200, "warmup": args.warmup, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) f32 Q/K/V projections, seeded",
+            "config": {"workload": "batch-1 decode step, attention part of every layer: KV append (RoPE, ring "
+                                   "write) + decode attention, counters advanced on the device",
+                       "parallelism": f"dp{world}"},
+            "detail": res, "peak_hbm_gbs": peaks["hbm_gbs"], "gpu_launches": 200 * (30 * 3 + 1)}
+
+
 # ---- reference arm ------------------------------------------------------------------
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -529,7 +592,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode", "kv_append"])
+    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode", "kv_append", "decode_step"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
@@ -563,8 +626,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
-        res = run_decode(args, rank, world, local) if args.workload == "decode" else \
-            run_kv_append(args, rank, world, local)
+        res = {"decode": run_decode, "kv_append": run_kv_append,
+               "decode_step": run_decode_step}[args.workload](args, rank, world, local)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

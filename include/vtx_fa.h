@@ -196,6 +196,9 @@ VTX_API int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *batch,
  *   per-token base array is given (one cache per stream in batched decode).
  * - q_out receives the rotated Q (it may equal q); with q_out NULL only K
  *   and V are processed.
+ * - Tokens of one call are written concurrently: two tokens of a call must
+ *   not target the same cache row (a prefill longer than the window writes
+ *   only its last `window` tokens).
  * positions, slots and the pointer arrays are device memory.  Asynchronous
  * on `stream`; no allocation. */
 typedef struct {
@@ -215,6 +218,17 @@ typedef struct {
     int32_t reserved[4];
 } vtx_kv_append_args;
 VTX_API int vtx_kv_append(const vtx_kv_append_args *args, void *stream);
+
+/* Advances the device-side decode counters of n streams by one token, so a
+ * captured decode step (vtx_kv_append + vtx_flash_attn_decode_batched per
+ * layer, then this) can be replayed token after token with no host work:
+ *   positions[i] += 1;  slots[i] = (slots[i] + 1) % window;
+ *   kv_len[i] = min(kv_len[i] + 1, window).
+ * Any of the three pointers may be NULL.  Replaces the host-side bookkeeping
+ * of run_decoder_step (kv_used += 1 and the shift-left when full,
+ * src/voxtral.cpp:2444-2471). */
+VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int32_t n, int32_t window,
+                               void *stream);
 
 /* Diagnostic: synchronises `stream`, returns and clears the device-side error
  * word of the current device (0 = none).  Kernels set it instead of hanging

@@ -448,22 +448,46 @@ fa_combine_kernel(const SplitArgs a, int gy)
     int nsp = a.n_splits;
     if (a.k_ptrs) nsp = max(1, min(a.n_splits, (a.kv_len[b] + a.chunk - 1) / a.chunk));
     const long long w0 = (((long long)b * gy + y) * a.n_qtiles + qt) * a.n_splits;
+    const float *ml = a.part_ml + (w0 * MAXR + r) * 2;             // split s at ml[s * MAXR * 2]
+    const float *po0 = a.part_o + (w0 * MAXR + r) * D;             // split s at po0[s * MAXR * D]
+    // maximum and sum over the splits, lanes taking splits lane, lane + 32, ...
     float M = -INFINITY;
-    for (int s = 0; s < nsp; ++s) M = fmaxf(M, a.part_ml[((w0 + s) * MAXR + r) * 2]);
+    for (int s = lane; s < nsp; s += 32) M = fmaxf(M, ml[(long long)s * MAXR * 2]);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
     const float Mu = M == -INFINITY ? 0.0f : M;
     float L = 0.0f;
+    for (int s = lane; s < nsp; s += 32) {
+        const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
+        L += l == 0.0f ? 0.0f : l * ex2(m - Mu);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
     constexpr int PL = D / 32;
     float o[PL];
 #pragma unroll
     for (int j = 0; j < PL; ++j) o[j] = 0.0f;
-    for (int s = 0; s < nsp; ++s) {
-        const float m = a.part_ml[((w0 + s) * MAXR + r) * 2];
-        const float l = a.part_ml[((w0 + s) * MAXR + r) * 2 + 1];
-        const float f = l == 0.0f ? 0.0f : ex2(m - Mu);
-        L += l * f;
-        const float *po = a.part_o + ((w0 + s) * MAXR + r) * D;
+    // O: splits four at a time so their loads are in flight together
+    int s = 0;
+    for (; s + 4 <= nsp; s += 4) {
+        float f[4], x[4][PL];
 #pragma unroll
-        for (int j = 0; j < PL; ++j) o[j] = fmaf(f, po[lane + 32 * j], o[j]);
+        for (int u = 0; u < 4; ++u) {
+            const float m = ml[(long long)(s + u) * MAXR * 2], l = ml[(long long)(s + u) * MAXR * 2 + 1];
+            f[u] = l == 0.0f ? 0.0f : ex2(m - Mu);
+#pragma unroll
+            for (int j = 0; j < PL; ++j) x[u][j] = po0[(long long)(s + u) * MAXR * D + lane + 32 * j];
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+            for (int j = 0; j < PL; ++j) o[j] = fmaf(f[u], x[u][j], o[j]);
+    }
+    for (; s < nsp; ++s) {
+        const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
+        const float f = l == 0.0f ? 0.0f : ex2(m - Mu);
+#pragma unroll
+        for (int j = 0; j < PL; ++j) o[j] = fmaf(f, po0[(long long)s * MAXR * D + lane + 32 * j], o[j]);
     }
     float *out = reinterpret_cast<float *>(a.dst + (long long)tok * a.d_nb2 + (long long)h * a.d_nb1 +
                                            (long long)b * a.d_nb3);

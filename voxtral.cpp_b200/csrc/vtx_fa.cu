@@ -153,9 +153,15 @@ int largest_divisor_le(int n, int cap) {
     return 1;
 }
 
-SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched) {
+// streaming: the work goes to the warp-per-item decode kernels (F16 / Q8_0),
+// whose splits need only be multiples of their 16-key stage.  Batched decode
+// is planned for max_kv (the caller's bound), not the lengths it will see, so
+// with few streams short caches would leave most of the GPU idle: streaming
+// plans aim at ~16 work items per SM at any length (32-key splits for one
+// stream over an 8192-row window), large batches keep their 1024-key chunks.
+SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched, bool streaming = false) {
     SplitPlan s{};
-    s.tk = g.kv_type == VTX_TYPE_F32 ? 32 : 64;
+    s.tk = streaming ? 16 : g.kv_type == VTX_TYPE_F32 ? 32 : 64;
     s.maxr = (g.n_q * g.G <= 4 && g.G <= 4) ? 4 : 16;
     s.hc = largest_divisor_le(g.G, s.maxr);
     s.n_hchunks = g.G / s.hc;
@@ -166,6 +172,7 @@ SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched) {
     const int max_tiles = (kv + s.tk - 1) / s.tk;
     long long want = (4LL * sms + base - 1) / base;     // ~4 CTAs per SM in flight
     if (batched) want = std::max<long long>(want, (kv + 1023) / 1024);
+    if (streaming) want = std::max<long long>(want, (16LL * sms + base - 1) / base);
     int n_splits = (int)std::min<long long>(std::max<long long>(want, 1), max_tiles);
     int chunk_tiles = (max_tiles + n_splits - 1) / n_splits;
     s.chunk = chunk_tiles * s.tk;
@@ -225,6 +232,17 @@ PrefillPlan plan_prefill(const Geo &g, const vtx_tensor *q, const vtx_tensor *k,
 }
 
 // ---- conversion kernel: K/V (F32 | F16 strided | Q8_0) -> packed f16 ---------
+
+// positions += 1, slots = (slots + 1) % window, kv_len = min(kv_len + 1, window)
+__global__ void decode_advance_kernel(int32_t *pos, int32_t *slots, int32_t *kv_len, int n, int window) {
+    grid_dep_wait();
+    grid_dep_launch();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    if (pos) pos[i] += 1;
+    if (slots) slots[i] = (slots[i] + 1) % window;
+    if (kv_len) kv_len[i] = min(kv_len[i] + 1, window);
+}
 
 __global__ void convert_kv_f16_kernel(const char *src, long long nb1, long long nb2, long long nb3, int type,
                                       int D, int n_kv, int H, int Bk, __half *dst) {
@@ -436,6 +454,20 @@ int pick_vec(int row, std::initializer_list<unsigned long long> vals) {
         if (ok) return v;
     }
     return 0;
+}
+
+// Whether a batched decode goes to the F16 streaming kernel (the same tests
+// as the dispatch below, from the batch description alone, so that the
+// workspace query and the call plan the same splits).
+bool batch_streaming(const vtx_decode_batch *b) {
+    const int G = b->n_head_q / b->n_head_kv;
+    if (G > 4) return false;
+    const int rb = row_bytes(b->kv_type, b->head_dim);
+    const int vec =
+        pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
+    // F16 only: a Q8_0 CTA covers all heads of a split with 211 KB of shared
+    // memory (one per SM), so its fixed cost needs the coarser default splits
+    return b->kv_type == VTX_TYPE_F16 && vec == 16;
 }
 
 template <int D, int NQT, bool HM, bool UF>
@@ -653,7 +685,7 @@ size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *b) {
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaGetLastError();
-    return plan_split(g, sms, g.n_kv, true).part_bytes;
+    return plan_split(g, sms, g.n_kv, true, batch_streaming(b)).part_bytes;
 }
 
 int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, size_t workspace_bytes, void *stream) {
@@ -671,7 +703,7 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
     const int D = b->head_dim;
     Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
           b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true);
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b));
     if (workspace_bytes < sp.part_bytes) return VTX_ERR_WORKSPACE;
     if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
     SplitArgs a{};
@@ -750,6 +782,17 @@ int vtx_kv_append(const vtx_kv_append_args *p, void *stream) {
                              : launch_pdl(kv_append_kernel<128>, dim3((unsigned)a.T), dim3(256), 0, st, a);
 }
 
+int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int32_t n, int32_t window,
+                       void *stream) {
+    if (n < 0 || window <= 0) return VTX_ERR_SHAPE;
+    if (n == 0 || (!positions && !slots && !kv_len)) return VTX_OK;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    return launch_pdl(decode_advance_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
+                      static_cast<cudaStream_t>(stream), positions, slots, kv_len, (int)n, (int)window);
+}
+
 int vtx_read_device_error(void *stream) {
     DeviceState *ds = nullptr;
     int rc = ensure_device(&ds);
@@ -822,7 +865,7 @@ extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, 
     const int D = b->head_dim;
     Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
           b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true);
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b));
     if (sp.part_bytes > (size_t)VTX_NOALLOC_SCRATCH_BYTES) return VTX_ERR_SCRATCH_LIMIT;
     void *scratch = nullptr;
     rc = noalloc_scratch(&scratch);

@@ -1,0 +1,113 @@
+"""Graph-replayed decode step for the attention part of voxtral.cpp's decoder.
+
+voxtral.cpp rebuilds, allocates and schedules a ggml graph for every decoded
+token (run_decoder_step, src/voxtral.cpp:2438-2473; graph build and
+scheduling :1921-1973, :2086-2101) and keeps the cache window with a host-side
+shift-left memmove (:1237-1266, :2444-2447).  This helper captures one step of
+the attention path for all layers once, as a CUDA graph:
+
+    for each layer:  vtx_kv_append          (RoPE of Q/K, K/V into the ring row)
+                     vtx_flash_attn_decode_batched   (attention over the ring)
+    then:            vtx_decode_advance     (positions, ring slots, lengths + 1)
+
+and replays it per token with no host work: positions, ring slots and key
+counts live on the device and advance inside the graph.  Each of the n_seq
+streams has its own cache per layer (rows = the window); the step's Q/K/V
+projections are read from fixed per-layer buffers that the caller (the rest
+of the decoder, out of scope here) fills before each replay.
+"""
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+
+import vtx_attn
+
+
+class DecodeStepGraph:
+    def __init__(self, n_layers: int, n_seq: int, n_head_q: int, n_head_kv: int, head_dim: int, kv_type: int,
+                 window: int, start_len, rope_base: float = 1e6, device: Optional[torch.device] = None):
+        """start_len: tokens already in each stream's cache (its prefill), one
+        int per stream; the next token goes to ring slot start_len % window at
+        position start_len."""
+        dev = device or torch.device("cuda", torch.cuda.current_device())
+        self.dev, self.L, self.S, self.Hq, self.Hkv, self.D = dev, n_layers, n_seq, n_head_q, n_head_kv, head_dim
+        self.kv_type, self.W, self.base = kv_type, window, rope_base
+        hb = head_dim // 32 * 34 if kv_type == vtx_attn.Q8_0 else head_dim * (4 if kv_type == vtx_attn.F32 else 2)
+        self.row = n_head_kv * hb
+        start = torch.as_tensor(start_len, dtype=torch.int32)
+        self.positions = start.clone().to(dev)
+        self.slots = (start % window).to(torch.int32).to(dev)
+        self.kv_len = torch.clamp(start + 1, max=window).to(torch.int32).to(dev)   # includes the new token
+        # caches: [layer][stream] of window rows
+        self.k_cache = torch.zeros((n_layers, n_seq, window, self.row), dtype=torch.uint8, device=dev)
+        self.v_cache = torch.zeros_like(self.k_cache)
+        self.k_ptrs = [torch.tensor([self.k_cache[l, s].data_ptr() for s in range(n_seq)], dtype=torch.int64,
+                                    device=dev) for l in range(n_layers)]
+        self.v_ptrs = [torch.tensor([self.v_cache[l, s].data_ptr() for s in range(n_seq)], dtype=torch.int64,
+                                    device=dev) for l in range(n_layers)]
+        # per-layer inputs (this step's projections) and outputs
+        self.q = torch.zeros((n_layers, n_seq, n_head_q, head_dim), device=dev)
+        self.k = torch.zeros((n_layers, n_seq, n_head_kv, head_dim), device=dev)
+        self.v = torch.zeros_like(self.k)
+        self.q_rot = torch.zeros_like(self.q)
+        self.out = torch.zeros_like(self.q)
+        self.plans: List[vtx_attn.DecodeBatchPlan] = []
+        for l in range(n_layers):
+            p = vtx_attn.DecodeBatchPlan([self.k_cache[l, s] for s in range(n_seq)],
+                                         [self.v_cache[l, s] for s in range(n_seq)], self.kv_len, n_head_q,
+                                         n_head_kv, head_dim, kv_type, self.row, hb, window, head_dim ** -0.5)
+            self.plans.append(p)
+        self.stream = torch.cuda.Stream(device=dev)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+    def fill(self, layer: int, seq: int, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor) -> None:
+        """Writes prefill tokens of one stream into one layer's ring (rows
+        positions % window; later tokens overwrite earlier ones, as the
+        reference's window keeps the most recent).  k, v: (T, Hkv, D) float32."""
+        if k.shape[0] > self.W:      # one call must not write a row twice: keep the most recent window
+            k, v, positions = k[-self.W:], v[-self.W:], positions[-self.W:]
+        pos = positions.to(device=self.dev, dtype=torch.int32)
+        vtx_attn.kv_append(k, v, pos, pos % self.W, self.k_cache[layer, seq], self.v_cache[layer, seq],
+                           self.kv_type, self.base, cache_nb1=self.row)
+
+    def _step_calls(self) -> None:
+        for l in range(self.L):
+            vtx_attn.kv_append(self.k[l], self.v[l], self.positions, self.slots, None, None, self.kv_type, self.base,
+                               q=self.q[l], q_out=self.q_rot[l], k_cache_ptrs=self.k_ptrs[l],
+                               v_cache_ptrs=self.v_ptrs[l], cache_nb1=self.row, stream=self.stream)
+            self.plans[l](self.q_rot[l], self.out[l], self.stream)
+        rc = vtx_attn.load().vtx_decode_advance(
+            vtx_attn.ctypes.c_void_p(self.positions.data_ptr()), vtx_attn.ctypes.c_void_p(self.slots.data_ptr()),
+            vtx_attn.ctypes.c_void_p(self.kv_len.data_ptr()), self.S, self.W,
+            vtx_attn.ctypes.c_void_p(self.stream.cuda_stream))
+        vtx_attn._check(rc, "vtx_decode_advance")
+
+    def step_eager(self) -> None:
+        """One step issued call by call from the host (the uncaptured path)."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.dev))
+        self._step_calls()
+        torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+
+    def capture(self) -> None:
+        torch.cuda.synchronize(self.dev)
+        self.graph = torch.cuda.CUDAGraph()
+        # the device counters must not move during capture: record only
+        with torch.cuda.graph(self.graph, stream=self.stream):
+            self._step_calls()
+        torch.cuda.synchronize(self.dev)
+
+    def step(self) -> None:
+        """One decode step for every stream and layer.  The first step runs
+        eagerly (it also performs the library's one-time per-device set-up,
+        which a capture must not contain) and is then captured; every later
+        step is a graph replay."""
+        if self.graph is None:
+            self.step_eager()
+            self.capture()
+            return
+        self.stream.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(self.stream):
+            self.graph.replay()
+        torch.cuda.current_stream(self.dev).wait_stream(self.stream)

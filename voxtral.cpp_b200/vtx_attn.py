@@ -102,6 +102,9 @@ def load(path: str = LIB_PATH):
     L.vtx_abi_version.restype = ctypes.c_int
     L.vtx_kv_append.argtypes = [P(KvAppendArgs), ctypes.c_void_p]
     L.vtx_kv_append.restype = ctypes.c_int
+    L.vtx_decode_advance.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
+                                     ctypes.c_int32, ctypes.c_void_p]
+    L.vtx_decode_advance.restype = ctypes.c_int
     _lib = L
     return L
 
