@@ -40,7 +40,7 @@ DEC = dict(n_seq=256, Hq=32, Hkv=8, D=128, lo=512, hi=16384)
 METRIC_ENC = "attn TFLOP/s (prefill/encoder)"
 ENC_TRAFFIC_BYTES = 11_581_696          # one encoder launch, from the committed ncu capture
 DEC_TRAFFIC_RATIO_F16 = (1_058_088_000 + 7_246_080) / 1_057_517_568   # (read + write) / KV bytes, 32 streams
-DEC_TRAFFIC_RATIO_Q8 = (562_370_304 + 6_304_000) / 561_806_208
+DEC_TRAFFIC_RATIO_Q8 = (562_400_768 + 6_991_872) / 561_806_208     # (read + write) / KV bytes, 32 streams
 METRIC_DEC = "KV GB/s (decode)"
 
 

@@ -158,11 +158,14 @@ def test_n_kv_zero_gives_zeros():
 
 # ---- ragged batched decode ----------------------------------------------------
 
-@pytest.mark.parametrize("kv", ["f16", "q8_0", "f32"])
-def test_decode_batched_ragged(kv):
+@pytest.mark.parametrize("kv,G", [("f16", 4), ("q8_0", 4), ("f32", 4), ("f16", 1), ("f16", 2), ("q8_0", 2)])
+def test_decode_batched_ragged(kv, G):
+    """Ragged batched decode; G < 4 leaves rows of the combine kernel's row
+    space idle, which its launch grid has to cover all the same."""
     import vtx_attn
-    rng = np.random.default_rng(21)
-    n_seq, Hq, Hkv, D = 12, 32, 8, 128
+    rng = np.random.default_rng(21 + G)
+    n_seq, Hkv, D = 12, 8, 128
+    Hq = G * Hkv
     lens = rng.integers(1, 3000, n_seq).astype(np.int32)
     lens[0] = 1
     qn = rng.standard_normal((n_seq, Hq, D)).astype(np.float32)
@@ -189,14 +192,16 @@ def test_decode_batched_ragged(kv):
     assert_close(got.cpu().numpy(), ref, f"batched decode {kv}")
 
 
-@pytest.mark.parametrize("Hkv", [2, 4])
-def test_decode_batched_q8_0_head_groups(Hkv):
+@pytest.mark.parametrize("Hkv,G", [(2, 4), (4, 4), (8, 1), (8, 3), (16, 2)])
+def test_decode_batched_q8_0_head_groups(Hkv, G):
     """Q8_0 streaming decode with fewer than 8 KV heads per token row (one CTA
-    copies 2 or 4 heads' slices), G = 4, lengths that need several splits."""
+    copies 2 or 4 heads' slices), with 16 (a CTA's 8 heads are half a token
+    row, so rows are copied one by one), and with GQA groups smaller than 4
+    (unused head columns of the score tile), lengths that need several splits."""
     import vtx_attn
-    rng = np.random.default_rng(30 + Hkv)
+    rng = np.random.default_rng(30 + Hkv + 10 * G)
     n_seq, D = 5, 128
-    Hq = 4 * Hkv
+    Hq = G * Hkv
     lens = np.array([1, 17, 1024, 2049, 4500], dtype=np.int32)
     qn = rng.standard_normal((n_seq, Hq, D)).astype(np.float32)
     ks = [O.quantize_q8_0(rng.standard_normal((int(L), Hkv, D)).astype(np.float32)) for L in lens]
@@ -209,7 +214,7 @@ def test_decode_batched_q8_0_head_groups(Hkv):
     got = plan(torch.from_numpy(qn).cuda())
     torch.cuda.synchronize()
     assert vtx_attn.read_device_error() == 0
-    assert_close(got.cpu().numpy(), ref, f"batched q8_0 decode Hkv={Hkv}")
+    assert_close(got.cpu().numpy(), ref, f"batched q8_0 decode Hkv={Hkv} G={G}")
 
 
 # ---- error paths through the C ABI ---------------------------------------------

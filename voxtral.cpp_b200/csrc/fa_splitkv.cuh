@@ -103,7 +103,7 @@ fa_splitkv_kernel(const SplitArgs a)
     using C = SplitCfg<D, KVT>;
     constexpr int TK = C::TK, PITCH = C::PITCH, STAGES = C::STAGES;
     constexpr int QP = D / 2 + 4;            // padded half-row of Q (floats)
-    extern __shared__ __align__(16) char smem[];
+    extern __shared__ __align__(128) char smem[];
     char *stage_base = smem;
     float *qs = reinterpret_cast<float *>(smem + STAGES * C::STAGE_BYTES);   // [MAXR][2][QP]
     float *ss = qs + MAXR * 2 * QP;                                            // [MAXR][TK]

@@ -334,6 +334,12 @@ void fill_math(float scale, float max_bias, float softcap, int Hq, float *qk_sca
     *qk_scale = softcap != 0.0f ? scale / softcap : scale;
 }
 
+// The combine kernel's row space: one warp per (stream, y, q tile, row of the
+// tile), rows past n_q or the group included; gy = KV heads x head chunks.
+long long combine_rows(const SplitArgs &a, long long gy) {
+    return (long long)a.B * gy * a.n_qtiles * a.tok_per_cta * a.hc;
+}
+
 template <int D, int KVT, int MAXR>
 int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
     constexpr int smem = splitkv_smem_bytes<D, KVT, MAXR>();
@@ -348,7 +354,7 @@ int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
     }
     if (launch_pdl(fa_splitkv_kernel<D, KVT, MAXR>, grid, dim3(128), smem, st, a) != VTX_OK) return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = (long long)a.B * grid.y * a.n_qtiles * a.tok_per_cta * a.hc;
+        const long long rows = combine_rows(a, grid.y);
         if (launch_pdl(fa_combine_kernel<D, MAXR>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a,
                        (int)grid.y) != VTX_OK)
             return VTX_ERR_CUDA;
@@ -380,7 +386,7 @@ int launch_decode_mma_t(const SplitArgs &a, cudaStream_t st) {
                    st, a, (int)items) != VTX_OK)
         return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = (long long)a.B * a.Hkv * a.G;
+        const long long rows = combine_rows(a, a.Hkv);
         if (launch_pdl(fa_combine_kernel<D, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
             VTX_OK)
             return VTX_ERR_CUDA;
@@ -422,7 +428,7 @@ int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
     if (launch_pdl(fa_decode_q8_kernel<128>, dim3((unsigned)items), dim3(C::NTHREADS), C::SMEM, st, a, hpc) != VTX_OK)
         return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = (long long)a.B * a.Hkv * a.G;
+        const long long rows = combine_rows(a, a.Hkv);
         if (launch_pdl(fa_combine_kernel<128, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
             VTX_OK)
             return VTX_ERR_CUDA;
