@@ -257,3 +257,90 @@ def window_mask(n: int, window: int = 750) -> np.ndarray:
     kj = np.arange(n)[None, :]
     allow = (kj <= qi) & (kj >= np.maximum(0, qi - (window - 1)))
     return np.where(allow, 0.0, -np.inf).astype(np.float16)
+
+
+# ---- realtime encoder chunking ---------------------------------------------------
+# Restates the chunk geometry of run_encoder_chunked (src/voxtral.cpp:2234-2335):
+# 3000 mel frames per chunk, 1500-frame stride, 750 overlapping encoder tokens
+# skipped in every chunk but the first (:26-27), token counts through the two
+# causal convolutions (compute_causal_conv1d_dims :1280-1297,
+# mel_frames_to_enc_tokens :1300-1305, downsample factor 4 from
+# include/voxtral.h:51).  Pinned against the reference's own token-count
+# functions compiled from their source (tests/golden/enc_chunks.json).
+
+ENC_CHUNK_MEL, ENC_CHUNK_OVERLAP, DOWNSAMPLE = 3000, 750, 4
+
+
+def causal_conv1d_out_len(in_len: int, kernel: int, stride: int) -> int:
+    """Output length of compute_causal_conv1d_dims (:1280-1297); its frame
+    count is float32 arithmetic, reproduced with numpy float32."""
+    if in_len <= 0 or kernel <= 0 or stride <= 0:
+        return 0
+    pad_total = kernel - stride
+    n_frames = np.float32(in_len - kernel + pad_total) / np.float32(stride) + np.float32(1.0)
+    target = (int(np.ceil(n_frames)) - 1) * stride + (kernel - pad_total)
+    padded = in_len + pad_total + max(0, target - in_len)
+    return (padded - kernel) // stride + 1
+
+
+def mel_frames_to_enc_tokens(n_frames: int) -> int:
+    """:1300-1305: conv0 (k 3, s 1), conv1 (k 3, s 2), truncated to a
+    multiple of the downsample factor."""
+    n = causal_conv1d_out_len(causal_conv1d_out_len(n_frames, 3, 1), 3, 2)
+    return n - n % DOWNSAMPLE
+
+
+def compute_total_enc_tokens(total_mel: int) -> int:
+    """:1308-1325: the stitched token count (the output allocation)."""
+    stride_mel = ENC_CHUNK_MEL - 2 * ENC_CHUNK_OVERLAP
+    total, off, first = 0, 0, True
+    while off < total_mel:
+        toks = mel_frames_to_enc_tokens(min(ENC_CHUNK_MEL, total_mel - off))
+        s = toks - (0 if first else ENC_CHUNK_OVERLAP)
+        if s <= 0:
+            break
+        total += s
+        off += stride_mel
+        first = False
+    return total
+
+
+def encoder_chunk_plan(total_mel: int):
+    """The chunks run_encoder_chunked processes, in order, as dicts with
+    mel_offset, mel_frames, n_tokens, skip, stride, rope_offset and
+    write_offset; plus (alloc_total, enc_seq_used)."""
+    alloc_total = compute_total_enc_tokens(total_mel)
+    chunks = []
+    if alloc_total <= 0:
+        return chunks, alloc_total, 0
+    stride_mel = ENC_CHUNK_MEL - 2 * ENC_CHUNK_OVERLAP
+    off, write, idx = 0, 0, 0
+    while off < total_mel:
+        frames = min(ENC_CHUNK_MEL, total_mel - off)
+        skip = ENC_CHUNK_OVERLAP if idx > 0 else 0
+        toks = mel_frames_to_enc_tokens(frames)
+        if toks - skip <= 0:                       # pre-check (:2265-2272)
+            break
+        stride = toks - skip
+        if stride <= 0:
+            break
+        if write + stride > alloc_total:           # clamp (:2307-2311)
+            stride = alloc_total - write
+            if stride <= 0:
+                break
+        chunks.append(dict(mel_offset=off, mel_frames=frames, n_tokens=toks, skip=skip, stride=stride,
+                           rope_offset=write - skip, write_offset=write))
+        write += stride
+        off += stride_mel
+        idx += 1
+    return chunks, alloc_total, write // DOWNSAMPLE * DOWNSAMPLE
+
+
+def encoder_stitch(chunk_out: np.ndarray, chunks, n_rows: int) -> np.ndarray:
+    """Host-side stitch as :2318-2328 does it: rows [skip, skip + stride) of
+    chunk c's output to rows [write_offset, write_offset + stride).
+    chunk_out: (n_chunks, chunk_rows, ...)."""
+    out = np.zeros((n_rows,) + chunk_out.shape[2:], dtype=chunk_out.dtype)
+    for c, ch in enumerate(chunks):
+        out[ch["write_offset"]:ch["write_offset"] + ch["stride"]] = chunk_out[c, ch["skip"]:ch["skip"] + ch["stride"]]
+    return out

@@ -424,76 +424,104 @@ fa_splitkv_kernel(const SplitArgs a)
     }
 }
 
-// Merge split partials: one warp per output row.
-template <int D, int MAXR>
-__global__ void __launch_bounds__(128)
+// Merge split partials: one CTA of NT threads per output row, so that at
+// batch 1 (a few dozen rows, up to hundreds of splits) the loads of all splits
+// are in flight together instead of one split after another.
+//   1. M = max over the splits' maxima (block reduction);
+//   2. thread (split group sg, float4 column c) sums f_s * o_s[c] over the
+//      splits s = sg, sg + NSG, ... with f_s = 2^(m_s - M) (0 for an empty
+//      split), and the block sums l_s * f_s;
+//   3. the NSG column partials are added in shared memory and scaled by 1/L.
+template <int D, int MAXR, int NT>
+__global__ void __launch_bounds__(NT)
 fa_combine_kernel(const SplitArgs a, int gy)
 {
     grid_dep_wait();
     grid_dep_launch();
-    const int lane = threadIdx.x & 31;
-    const long long row_id = (long long)blockIdx.x * 4 + (threadIdx.x >> 5);
+    constexpr int C4 = D / 4, NSG = NT / C4, NW = NT / 32;   // float4 columns, split groups, warps
+    __shared__ float red_m[NW], red_l[NW];
+    __shared__ float4 acc_s[NSG][C4];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const long long row_id = blockIdx.x;
     const int rows = a.tok_per_cta * a.hc;
-    const long long total = (long long)a.B * gy * a.n_qtiles * rows;
-    if (row_id >= total) return;
     const int r = (int)(row_id % rows);
     long long t = row_id / rows;
     const int qt = (int)(t % a.n_qtiles); t /= a.n_qtiles;
     const int y = (int)(t % gy);
     const int b = (int)(t / gy);
+    if (b >= a.B) return;
     const int hchunk = y % a.n_hchunks, g = y / a.n_hchunks;
     const int tok = qt * a.tok_per_cta + r / a.hc;
-    if (tok >= a.n_q) return;
+    if (tok >= a.n_q) return;                                  // uniform over the CTA
     const int h = g * a.G + hchunk * a.hc + r % a.hc;
     int nsp = a.n_splits;
     if (a.k_ptrs) nsp = max(1, min(a.n_splits, (a.kv_len[b] + a.chunk - 1) / a.chunk));
     const long long w0 = (((long long)b * gy + y) * a.n_qtiles + qt) * a.n_splits;
     const float *ml = a.part_ml + (w0 * MAXR + r) * 2;             // split s at ml[s * MAXR * 2]
     const float *po0 = a.part_o + (w0 * MAXR + r) * D;             // split s at po0[s * MAXR * D]
-    // maximum and sum over the splits, lanes taking splits lane, lane + 32, ...
+
     float M = -INFINITY;
-    for (int s = lane; s < nsp; s += 32) M = fmaxf(M, ml[(long long)s * MAXR * 2]);
+    for (int s = tid; s < nsp; s += NT) M = fmaxf(M, ml[(long long)s * MAXR * 2]);
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+    if (lane == 0) red_m[warp] = M;
+    __syncthreads();
+#pragma unroll
+    for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w]);
     const float Mu = M == -INFINITY ? 0.0f : M;
+
     float L = 0.0f;
-    for (int s = lane; s < nsp; s += 32) {
+    for (int s = tid; s < nsp; s += NT) {
         const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
         L += l == 0.0f ? 0.0f : l * ex2(m - Mu);
     }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    constexpr int PL = D / 32;
-    float o[PL];
-#pragma unroll
-    for (int j = 0; j < PL; ++j) o[j] = 0.0f;
-    // O: splits four at a time so their loads are in flight together
-    int s = 0;
-    for (; s + 4 <= nsp; s += 4) {
-        float f[4], x[4][PL];
+    const int c = tid % C4, sg = tid / C4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    int s = sg;
+    for (; s + 3 * NSG < nsp; s += 4 * NSG) {                   // four splits' loads in flight per thread
+        float f[4];
+        float4 x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
-            const float m = ml[(long long)(s + u) * MAXR * 2], l = ml[(long long)(s + u) * MAXR * 2 + 1];
+            const long long su = s + u * NSG;
+            const float m = ml[su * MAXR * 2], l = ml[su * MAXR * 2 + 1];
             f[u] = l == 0.0f ? 0.0f : ex2(m - Mu);
-#pragma unroll
-            for (int j = 0; j < PL; ++j) x[u][j] = po0[(long long)(s + u) * MAXR * D + lane + 32 * j];
+            x[u] = reinterpret_cast<const float4 *>(po0 + su * MAXR * D)[c];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u)
-#pragma unroll
-            for (int j = 0; j < PL; ++j) o[j] = fmaf(f[u], x[u][j], o[j]);
+        for (int u = 0; u < 4; ++u) {
+            acc.x = fmaf(f[u], x[u].x, acc.x); acc.y = fmaf(f[u], x[u].y, acc.y);
+            acc.z = fmaf(f[u], x[u].z, acc.z); acc.w = fmaf(f[u], x[u].w, acc.w);
+        }
     }
-    for (; s < nsp; ++s) {
+    for (; s < nsp; s += NSG) {
         const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
         const float f = l == 0.0f ? 0.0f : ex2(m - Mu);
-#pragma unroll
-        for (int j = 0; j < PL; ++j) o[j] = fmaf(f, po0[(long long)s * MAXR * D + lane + 32 * j], o[j]);
+        const float4 x = reinterpret_cast<const float4 *>(po0 + (long long)s * MAXR * D)[c];
+        acc.x = fmaf(f, x.x, acc.x); acc.y = fmaf(f, x.y, acc.y);
+        acc.z = fmaf(f, x.z, acc.z); acc.w = fmaf(f, x.w, acc.w);
     }
-    float *out = reinterpret_cast<float *>(a.dst + (long long)tok * a.d_nb2 + (long long)h * a.d_nb1 +
-                                           (long long)b * a.d_nb3);
-    const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+    acc_s[sg][c] = acc;
 #pragma unroll
-    for (int j = 0; j < PL; ++j) out[lane + 32 * j] = o[j] * inv;
+    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+    if (lane == 0) red_l[warp] = L;
+    __syncthreads();
+    if (tid < C4) {
+        L = 0.0f;
+#pragma unroll
+        for (int w = 0; w < NW; ++w) L += red_l[w];
+        float4 o = acc_s[0][tid];
+#pragma unroll
+        for (int q = 1; q < NSG; ++q) {
+            const float4 v = acc_s[q][tid];
+            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+        }
+        const float inv = L == 0.0f ? 0.0f : 1.0f / L;
+        float *out = reinterpret_cast<float *>(a.dst + (long long)tok * a.d_nb2 + (long long)h * a.d_nb1 +
+                                               (long long)b * a.d_nb3);
+        out[4 * tid + 0] = o.x * inv; out[4 * tid + 1] = o.y * inv;
+        out[4 * tid + 2] = o.z * inv; out[4 * tid + 3] = o.w * inv;
+    }
 }
 
 template <int D, int KVT, int MAXR>

@@ -15,8 +15,10 @@
 // angles are the same floats ggml uses; cos/sin are taken in double and
 // rounded to float (the correctly rounded values).
 //
-// One CTA per token builds its cos/sin table once; a warp streams one row
-// (tensor, head) at a time, a lane owning head_dim/32 consecutive elements.
+// A CTA per token (many tokens) or per (token, 8 rows) (a few tokens: a
+// decode step) builds the token's cos/sin table when it holds a Q or K row;
+// each warp streams one row (tensor, head) at a time, a lane owning
+// head_dim/32 consecutive elements.
 // Cache types: F32 (the reference's own cache), F16 (round to nearest even)
 // and Q8_0 (per 32 values d = amax/127 stored as f16,
 // q = round-half-even(x * 127/amax), as ggml's CPU from_float; a block is
@@ -39,11 +41,13 @@ struct KvAppendArgs {
     char *k_cache, *v_cache;
     const void *const *k_ptrs; const void *const *v_ptrs;   // optional per-token cache bases
     long long cache_nb1;                    // bytes per cache row
+    int rows_per_cta;                       // rows of a token one CTA handles
 };
 
-// One CTA per token: threads 0..D/2-1 build the token's cos/sin table in
-// shared memory (thread i runs the float angle recurrence i steps, then one
-// double-precision sincos rounded to float), then 8 warps stream the token's
+// Grid (tokens, ceil((Hq + 2 Hkv) / rows_per_cta)), 8 warps: threads
+// 0..D/2-1 build the token's cos/sin table in shared memory (thread i runs
+// the float angle recurrence i steps, then one double-precision sincos
+// rounded to float), then the warps take the CTA's rows of the token's
 // Hq + 2 Hkv rows, one row per warp at a time.
 template <int D>
 __global__ void __launch_bounds__(256)
@@ -55,7 +59,11 @@ kv_append_kernel(const KvAppendArgs a)
     __shared__ float2 cs[D / 2];                            // (cos, sin) of pair i
     const int t = blockIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    if (threadIdx.x < D / 2) {
+    // rows of a token: Q heads, then K heads, then V heads; this CTA takes
+    // rows [r0, r0 + rows_per_cta), a warp per row at a time
+    const int nwarps = blockDim.x >> 5, r0 = blockIdx.y * a.rows_per_cta;
+    const bool rope = r0 < a.Hq + a.Hkv;                     // some Q or K row here
+    if (rope && threadIdx.x < D / 2) {
         float theta = (float)a.positions[t];
         for (int i = 0; i < (int)threadIdx.x; ++i) theta *= a.theta_scale;
         double sd, cd;
@@ -65,7 +73,7 @@ kv_append_kernel(const KvAppendArgs a)
     __syncthreads();
     const int slot = a.slots[t];
     const int per_tok = a.Hq + 2 * a.Hkv;
-    for (int r = warp; r < per_tok; r += blockDim.x >> 5) {
+    for (int r = r0 + warp; r < min(r0 + a.rows_per_cta, per_tok); r += nwarps) {
         const int kind = r < a.Hq ? 0 : (r < a.Hq + a.Hkv ? 1 : 2);   // Q, K, V
         const int h = kind == 0 ? r : (kind == 1 ? r - a.Hq : r - a.Hq - a.Hkv);
         const float *src = kind == 0 ? a.q + (long long)t * a.q_nb1

@@ -159,9 +159,13 @@ int largest_divisor_le(int n, int cap) {
 // with few streams short caches would leave most of the GPU idle: streaming
 // plans aim at ~16 work items per SM at any length (32-key splits for one
 // stream over an 8192-row window), large batches keep their 1024-key chunks.
-SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched, bool streaming = false) {
+// streaming: the F16 decode kernel (a warp per head and split) runs.
+// q8_ctas: the Q8_0 decode kernel runs with this many CTAs per key split
+// (streams x head groups); each CTA holds an SM, so the keys are split for
+// about one CTA per SM, in 16-key stages, at least two stages per CTA.
+SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched, bool streaming = false, int q8_ctas = 0) {
     SplitPlan s{};
-    s.tk = streaming ? 16 : g.kv_type == VTX_TYPE_F32 ? 32 : 64;
+    s.tk = (streaming || q8_ctas) ? 16 : g.kv_type == VTX_TYPE_F32 ? 32 : 64;
     s.maxr = (g.n_q * g.G <= 4 && g.G <= 4) ? 4 : 16;
     s.hc = largest_divisor_le(g.G, s.maxr);
     s.n_hchunks = g.G / s.hc;
@@ -173,8 +177,10 @@ SplitPlan plan_split(const Geo &g, int sms, int max_kv, bool batched, bool strea
     long long want = (4LL * sms + base - 1) / base;     // ~4 CTAs per SM in flight
     if (batched) want = std::max<long long>(want, (kv + 1023) / 1024);
     if (streaming) want = std::max<long long>(want, (16LL * sms + base - 1) / base);
+    if (q8_ctas) want = std::max<long long>((sms + q8_ctas - 1) / q8_ctas, batched ? (kv + 1023) / 1024 : 1);
     int n_splits = (int)std::min<long long>(std::max<long long>(want, 1), max_tiles);
     int chunk_tiles = (max_tiles + n_splits - 1) / n_splits;
+    if (q8_ctas) chunk_tiles = std::max(chunk_tiles, 2);
     s.chunk = chunk_tiles * s.tk;
     s.n_splits = (kv + s.chunk - 1) / s.chunk;
     s.part_bytes = 0;
@@ -336,8 +342,17 @@ void fill_math(float scale, float max_bias, float softcap, int Hq, float *qk_sca
 
 // The combine kernel's row space: one warp per (stream, y, q tile, row of the
 // tile), rows past n_q or the group included; gy = KV heads x head chunks.
-long long combine_rows(const SplitArgs &a, long long gy) {
-    return (long long)a.B * gy * a.n_qtiles * a.tok_per_cta * a.hc;
+// The combine kernel's row space: one CTA per (stream, y, q tile, row of the
+// tile), rows past n_q or the group included; gy = KV heads x head chunks.
+// Many splits (a few streams): 512 threads, so each thread merges few splits.
+template <int D, int MAXR>
+int launch_combine(const SplitArgs &a, int gy, cudaStream_t st) {
+    const long long rows = (long long)a.B * gy * a.n_qtiles * a.tok_per_cta * a.hc;
+    if (rows > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
+    const int rc = a.n_splits > 32
+                       ? launch_pdl(fa_combine_kernel<D, MAXR, 512>, dim3((unsigned)rows), dim3(512), 0, st, a, gy)
+                       : launch_pdl(fa_combine_kernel<D, MAXR, 128>, dim3((unsigned)rows), dim3(128), 0, st, a, gy);
+    return rc == VTX_OK ? VTX_OK : VTX_ERR_CUDA;
 }
 
 template <int D, int KVT, int MAXR>
@@ -354,10 +369,7 @@ int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
     }
     if (launch_pdl(fa_splitkv_kernel<D, KVT, MAXR>, grid, dim3(128), smem, st, a) != VTX_OK) return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = combine_rows(a, grid.y);
-        if (launch_pdl(fa_combine_kernel<D, MAXR>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a,
-                       (int)grid.y) != VTX_OK)
-            return VTX_ERR_CUDA;
+        return launch_combine<D, MAXR>(a, (int)grid.y, st);
     }
     return VTX_OK;
 }
@@ -386,10 +398,7 @@ int launch_decode_mma_t(const SplitArgs &a, cudaStream_t st) {
                    st, a, (int)items) != VTX_OK)
         return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = combine_rows(a, a.Hkv);
-        if (launch_pdl(fa_combine_kernel<D, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
-            VTX_OK)
-            return VTX_ERR_CUDA;
+        return launch_combine<D, 4>(a, a.Hkv, st);
     }
     return VTX_OK;
 }
@@ -428,10 +437,7 @@ int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
     if (launch_pdl(fa_decode_q8_kernel<128>, dim3((unsigned)items), dim3(C::NTHREADS), C::SMEM, st, a, hpc) != VTX_OK)
         return VTX_ERR_CUDA;
     if (!a.write_final) {
-        const long long rows = combine_rows(a, a.Hkv);
-        if (launch_pdl(fa_combine_kernel<128, 4>, dim3((unsigned)((rows + 3) / 4)), dim3(128), 0, st, a, a.Hkv) !=
-            VTX_OK)
-            return VTX_ERR_CUDA;
+        return launch_combine<128, 4>(a, a.Hkv, st);
     }
     return VTX_OK;
 }
@@ -465,6 +471,15 @@ int pick_vec(int row, std::initializer_list<unsigned long long> vals) {
 // Whether a batched decode goes to the F16 streaming kernel (the same tests
 // as the dispatch below, from the batch description alone, so that the
 // workspace query and the call plan the same splits).
+// CTAs per key split when the Q8_0 decode kernel will run for this batch, else 0.
+int batch_q8_ctas(const vtx_decode_batch *b) {
+    const int G = b->n_head_q / b->n_head_kv;
+    const int hpc = decode_q8_hpc(b->kv_type, b->head_dim, 1, G, b->n_head_kv, G <= 4 ? 4 : 16, 1,
+                                  (long long)b->kv_nb1, (long long)b->kv_nb2, (long long)b->kv_nb1,
+                                  (long long)b->kv_nb2);
+    return hpc ? b->n_seq * (b->n_head_kv / hpc) : 0;
+}
+
 bool batch_streaming(const vtx_decode_batch *b) {
     const int G = b->n_head_q / b->n_head_kv;
     if (G > 4) return false;
@@ -691,7 +706,7 @@ size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *b) {
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaGetLastError();
-    return plan_split(g, sms, g.n_kv, true, batch_streaming(b)).part_bytes;
+    return plan_split(g, sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b)).part_bytes;
 }
 
 int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, size_t workspace_bytes, void *stream) {
@@ -709,7 +724,7 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
     const int D = b->head_dim;
     Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
           b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b));
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b));
     if (workspace_bytes < sp.part_bytes) return VTX_ERR_WORKSPACE;
     if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
     SplitArgs a{};
@@ -760,6 +775,7 @@ int vtx_kv_append(const vtx_kv_append_args *p, void *stream) {
     if ((!p->k_cache && !p->k_cache_ptrs) || (!p->v_cache && !p->v_cache_ptrs)) return VTX_ERR_NULL;
     if (p->q_out && (!p->q || p->n_head_q <= 0)) return VTX_ERR_NULL;
     if (!(p->freq_base > 0.0f)) return VTX_ERR_SHAPE;
+    if ((long long)p->n_head_q + 2LL * p->n_head_kv > 8LL * 65535) return VTX_ERR_UNSUPPORTED;   // grid.y
     // float2 row loads / stores; half2 (F16) or 2-byte (Q8_0) cache stores
     const uintptr_t rows = reinterpret_cast<uintptr_t>(p->k) | reinterpret_cast<uintptr_t>(p->v) | p->k_nb1 |
                            p->v_nb1 | (p->q_out ? reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->q_out) |
@@ -784,8 +800,13 @@ int vtx_kv_append(const vtx_kv_append_args *p, void *stream) {
     a.k_ptrs = p->k_cache_ptrs; a.v_ptrs = p->v_cache_ptrs;
     a.cache_nb1 = (long long)p->cache_nb1;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return p->head_dim == 64 ? launch_pdl(kv_append_kernel<64>, dim3((unsigned)a.T), dim3(256), 0, st, a)
-                             : launch_pdl(kv_append_kernel<128>, dim3((unsigned)a.T), dim3(256), 0, st, a);
+    // a decode step's few tokens: 8 rows (one per warp) per CTA, so the rows are
+    // in flight together; many tokens: one CTA per token, one table build each
+    const int per_tok = a.Hq + 2 * a.Hkv;
+    a.rows_per_cta = a.T >= 2 * ds->sms ? per_tok : 8;
+    const dim3 grid((unsigned)a.T, (unsigned)((per_tok + a.rows_per_cta - 1) / a.rows_per_cta));
+    return p->head_dim == 64 ? launch_pdl(kv_append_kernel<64>, grid, dim3(256), 0, st, a)
+                             : launch_pdl(kv_append_kernel<128>, grid, dim3(256), 0, st, a);
 }
 
 int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int32_t n, int32_t window,
@@ -871,7 +892,7 @@ extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, 
     const int D = b->head_dim;
     Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
           b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b));
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b));
     if (sp.part_bytes > (size_t)VTX_NOALLOC_SCRATCH_BYTES) return VTX_ERR_SCRATCH_LIMIT;
     void *scratch = nullptr;
     rc = noalloc_scratch(&scratch);
