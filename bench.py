@@ -1,7 +1,7 @@
 """Benchmark of the voxtral.cpp attention node on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vtx|reference]
-                    [--workload encoder|decode]
+                    [--workload encoder|decode|kv_append|decode_step|realtime]
 
 Headline workload: the Whisper-large-shaped audio
 encoder self-attention of voxtral.cpp (src/voxtral.cpp:1611): one 30 s clip ->
@@ -13,7 +13,11 @@ attention TFLOP/s = 4 * D * H * n_q * n_kv * layers / time.
 
 --workload decode times configs[4] instead: 256 ragged streams (n_kv ~ U[512,
 16384]), GQA 32/8 x 128, f16 KV, one decode token per stream; one step = one
-layer's attention for all streams (KV GB/s).
+layer's attention for all streams (KV GB/s).  kv_append and decode_step time
+the decoder's cache update and the graph-replayed batch-1 decode step
+(configs[2], configs[3]); realtime times configs[3] end to end on the
+attention path: 10 min of audio as chunked windowed encoder attention, the
+chunk stitch and 7461 Q8_0 decode steps (audio-sec/sec).
 
 Multi-GPU: one process per GPU (torchrun); each rank attends its own clips /
 streams (weak scaling, no collective on the data path); time = max over ranks.
@@ -561,6 +565,117 @@ def run_decode_step(args, rank, world, local):
             "detail": res, "peak_hbm_gbs": peaks["hbm_gbs"], "gpu_launches": 200 * (30 * 3 + 1)}
 
 
+# ---- realtime long-form streaming, attention path --------------------
+def run_realtime(args, rank, world, local):
+    """The attention work of 10 minutes of synthetic audio through the realtime
+    model, per GPU (one independent utterance per rank):
+      encoder: 60000 mel frames -> 39 chunks of <= 1500 tokens
+               (vtx_encoder_chunk_plan, src/voxtral.cpp:2234-2335); each of the
+               32 layers is ONE vtx_flash_attn_ext call with the chunks on the
+               batch axis (32 heads x 64, causal + window 750, f16 Q/K/V per
+               layer), then vtx_encoder_stitch gathers the chunks' new rows
+               (the last layer's attention rows stand in for the encoder
+               output that the reference stitches through host memory);
+      decoder: 7500 tokens (one per 80 ms) over 26 layers, GQA 32/8 x 128,
+               Q8_0 ring cache growing from 39 tokens: DecodeStepGraph replays
+               (KV append + decode attention per layer, device counters).
+    One step = the whole 10 minutes; value = audio-sec/sec = 600 x ranks /
+    (max over ranks of the step time)."""
+    import torch
+    import vtx_attn
+    from decode_step import DecodeStepGraph
+
+    dev = torch.device("cuda", local)
+    audio_s, mel = 600.0, 60000
+    H, D, W, L_enc = 32, 64, 750, 32
+    L_dec, start, n_tok = 26, 39, 7500
+    chunks, total, used = vtx_attn.encoder_chunk_plan(mel)
+    C = len(chunks)
+    n = max(c.n_tokens for c in chunks)                       # 1500: shorter last chunks are padded (causal)
+    g = torch.Generator(device=dev)
+    g.manual_seed(303 + rank)
+    # two alternating Q/K/V sets: one layer's 690 MB is far above L2 already
+    qkv = torch.empty((2, 3, C, n, H, D), dtype=torch.float16, device=dev)
+    for i in range(2):
+        for j in range(3):
+            qkv[i, j].copy_(torch.randn((C, n, H, D), generator=g, device=dev))
+    out = torch.empty((C, n, H, D), device=dev)
+    stitched = torch.empty((total, H * D), device=dev)
+    views = [[qkv[l % 2, i].permute(0, 2, 1, 3) for i in range(3)] for l in range(L_enc)]   # (C, H, n, D)
+    stream = torch.cuda.Stream(device=dev)
+
+    def encoder():
+        for l in range(L_enc):
+            q, k, v = views[l]
+            vtx_attn.flash_attn_ext(q, k, v, None, D ** -0.5, causal=True, window=W, out=out, stream=stream)
+        vtx_attn.encoder_stitch(out.view(C, n, H * D), chunks, stitched, stream=stream)
+
+    dec = DecodeStepGraph(L_dec, 1, DEC["Hq"], DEC["Hkv"], DEC["D"], vtx_attn.Q8_0, 8192, [start], device=dev)
+    for l in range(L_dec):
+        k = torch.randn((start, DEC["Hkv"], DEC["D"]), generator=g, device=dev)
+        dec.fill(l, 0, k, torch.randn_like(k), torch.arange(start, dtype=torch.int32))
+    dec.q.normal_(generator=g)
+    dec.k.normal_(generator=g)
+    dec.v.normal_(generator=g)
+    dec.step()                                                # eager first step + graph capture
+    torch.cuda.synchronize()
+    steps_dec = n_tok - start
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def pipeline(record: bool):
+        dec.reset()
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        if record:
+            ev[0].record(stream)
+        encoder()
+        if record:
+            ev[1].record(stream)
+        dec.stream.wait_stream(stream)
+        for _ in range(steps_dec):
+            dec.step()
+        stream.wait_stream(dec.stream)
+        if record:
+            ev[2].record(stream)
+
+    for _ in range(max(3, args.warmup)):
+        pipeline(False)
+    torch.cuda.synchronize()
+    t_enc = t_dec = 0.0
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        for _ in range(args.steps):
+            pipeline(True)
+            torch.cuda.synchronize()
+            t_enc += ev[0].elapsed_time(ev[1])
+            t_dec += ev[1].elapsed_time(ev[2])
+        barrier(world)
+    ms_local = (t_enc + t_dec) / args.steps
+    ms = barrier_max(ms_local, world)
+    pairs = sum(sum(min(i + 1, W) for i in range(c.n_tokens)) for c in chunks)
+    enc_flop = 4.0 * D * H * pairs * L_enc
+    kv_row = DEC["Hkv"] * (DEC["D"] // 32 * 34)
+    dec_bytes = L_dec * kv_row * 2 * sum(min(t + 1, 8192) for t in range(start, n_tok))
+    e_ms, d_ms = t_enc / args.steps, t_dec / args.steps
+    return {"metric": "audio-sec/sec (realtime model, attention path)",
+            "value": round(audio_s * world / (ms * 1e-3), 1), "unit": "audio-s/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": round(ms, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16 encoder / q8_0 KV",
+            "data": "synthetic N(0,1) Q/K/V, seeded per rank (10 min of audio per rank)",
+            "config": {"workload": f"configs[3] realtime: {audio_s:.0f} s audio = {mel} mel frames -> {C} encoder "
+                                   f"chunks ({total} tokens, 32 layers, 32 heads x 64, causal + window 750, one "
+                                   f"batched call per layer) + chunk stitch; {n_tok - start} decode steps x 26 "
+                                   f"layers, GQA 32/8 x 128, Q8_0 ring cache {start} -> {n_tok} keys",
+                       "l2": "an encoder layer reads 690 MB of Q/K/V (two alternating sets); the decoder reads "
+                             "26 layers' caches (up to 424 MB) per token",
+                       "parallelism": f"dp{world} (one utterance per GPU)"},
+            "detail": {"encoder_ms": round(e_ms, 2), "encoder_tflops": round(enc_flop / (e_ms * 1e-3) / 1e12, 1),
+                       "decoder_ms": round(d_ms, 2), "decoder_us_per_token": round(d_ms * 1e3 / (n_tok - start), 1),
+                       "decoder_kv_GBps": round(dec_bytes / (d_ms * 1e-3) / 1e9, 1), "chunks": C,
+                       "enc_tokens": total},
+            "gpu_launches": args.steps * (L_enc + 1 + (n_tok - start) * (L_dec * 3 + 1)),
+            "clocks": clocks.summary()}
+
+
 # ---- reference arm ------------------------------------------------------------------
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
@@ -594,7 +709,8 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
-    ap.add_argument("--workload", default="encoder", choices=["encoder", "decode", "kv_append", "decode_step"])
+    ap.add_argument("--workload", default="encoder",
+                    choices=["encoder", "decode", "kv_append", "decode_step", "realtime"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
@@ -628,8 +744,8 @@ def main():
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
-        res = {"decode": run_decode, "kv_append": run_kv_append,
-               "decode_step": run_decode_step}[args.workload](args, rank, world, local)
+        res = {"decode": run_decode, "kv_append": run_kv_append, "decode_step": run_decode_step,
+               "realtime": run_realtime}[args.workload](args, rank, world, local)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()

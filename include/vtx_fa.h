@@ -230,6 +230,46 @@ VTX_API int vtx_kv_append(const vtx_kv_append_args *args, void *stream);
 VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int32_t n, int32_t window,
                                void *stream);
 
+/* ---- realtime encoder: chunk plan and device-side stitch ------------------ */
+
+/* One chunk of the realtime model's chunked encoder run (run_encoder_chunked,
+ * src/voxtral.cpp:2234-2335): chunks of 3000 mel frames every 1500 frames;
+ * every chunk but the first skips the 750 encoder tokens that overlap the
+ * previous one (:26-27).  Token counts follow mel_frames_to_enc_tokens
+ * (:1300-1305: two causal convolutions, then a multiple of 4). */
+typedef struct vtx_enc_chunk {
+    int32_t mel_offset;       /* first mel frame of the chunk */
+    int32_t mel_frames;       /* mel frames in the chunk, <= 3000 */
+    int32_t n_tokens;         /* encoder tokens of the chunk (its attention length) */
+    int32_t skip;             /* leading tokens already produced by the previous chunk */
+    int32_t stride;           /* tokens the chunk adds to the stitched output */
+    int32_t rope_offset;      /* absolute position of the chunk's token 0 */
+    int32_t write_offset;     /* stitched-output row of the chunk's token `skip` */
+    int32_t reserved;
+} vtx_enc_chunk;
+
+/* Plans the chunks of an utterance of total_mel_frames mel frames, exactly as
+ * run_encoder_chunked walks them (including its early stop and its clamp to
+ * compute_total_enc_tokens, :1308-1325).  Writes min(n, max_chunks) entries
+ * (chunks may be NULL to query n) and returns n >= 0, or a negative
+ * vtx_status.  *n_tokens_total (optional) gets the stitched token count (the
+ * reference's output allocation); *n_tokens_used (optional) that count
+ * trimmed to a multiple of the downsample factor (enc_seq_used, :2331-2332).
+ * Host only: no CUDA call, no allocation. */
+VTX_API int vtx_encoder_chunk_plan(int32_t total_mel_frames, vtx_enc_chunk *chunks, int32_t max_chunks,
+                                   int32_t *n_tokens_total, int32_t *n_tokens_used);
+
+/* Stitches per-chunk encoder rows into the long-form output on the device,
+ * replacing the device -> host -> device copy of :2318-2328: for each chunk c,
+ * rows [skip, skip + stride) of chunk c (src + c * src_chunk_bytes
+ * + row * src_row_bytes) are copied to rows [write_offset, write_offset +
+ * stride) of dst (row pitch dst_row_bytes), row_bytes bytes per row.  chunks
+ * is the host array from vtx_encoder_chunk_plan.  One kernel launch per 64
+ * chunks on `stream`; no allocation, no host sync, graph-capturable. */
+VTX_API int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t src_row_bytes, void *dst,
+                               size_t dst_row_bytes, size_t row_bytes, const vtx_enc_chunk *chunks,
+                               int32_t n_chunks, void *stream);
+
 /* Diagnostic: synchronises `stream`, returns and clears the device-side error
  * word of the current device (0 = none).  Kernels set it instead of hanging
  * when a bounded pipeline wait runs out, or when a batched-decode stream base

@@ -29,7 +29,8 @@ def test_header_declares_the_entry_points():
     syms = set(declared_symbols())
     assert {"vtx_flash_attn_ext", "vtx_flash_attn_ext_workspace", "vtx_flash_attn_decode_batched",
             "vtx_flash_attn_decode_batched_workspace", "vtx_strerror", "vtx_abi_version",
-            "vtx_read_device_error", "vtx_flash_attn_decode_batched_noalloc", "vtx_kv_append"} <= syms
+            "vtx_read_device_error", "vtx_flash_attn_decode_batched_noalloc", "vtx_kv_append",
+            "vtx_decode_advance", "vtx_encoder_chunk_plan", "vtx_encoder_stitch"} <= syms
 
 
 def test_library_exports_every_declared_symbol(lib):

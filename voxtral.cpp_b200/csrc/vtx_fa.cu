@@ -28,6 +28,7 @@
 #include "fa_decode_mma.cuh"
 #include "fa_decode_q8.cuh"
 #include "kv_append.cuh"
+#include "enc_stitch.cuh"
 
 using namespace vtx;
 
@@ -235,6 +236,40 @@ PrefillPlan plan_prefill(const Geo &g, const vtx_tensor *q, const vtx_tensor *k,
     p.n_cta_q = (p.n_tiles_q + p.nqt - 1) / p.nqt;
     if (p.convert) p.conv_bytes = 2 * align_up((size_t)g.Bkv * g.Hkv * g.n_kv * g.D * 2, 256);
     return p;
+}
+
+// ---- realtime encoder chunk geometry (host) -------------------------------------
+// Chunk constants of src/voxtral.cpp:26-27 and the downsample factor of
+// include/voxtral.h:51.
+constexpr int kEncChunkMel = 3000, kEncChunkOverlap = 750, kEncDownsample = 4;
+
+// Output length of one causal convolution (compute_causal_conv1d_dims,
+// src/voxtral.cpp:1280-1297); the frame count is float arithmetic there too.
+int causal_conv_out_len(int in_len, int kernel, int stride) {
+    if (in_len <= 0 || kernel <= 0 || stride <= 0) return 0;
+    const int pad = kernel - stride;
+    const float frames = (float)(in_len - kernel + pad) / (float)stride + 1.0f;
+    const int target = ((int)std::ceil(frames) - 1) * stride + (kernel - pad);
+    const int padded = in_len + pad + std::max(0, target - in_len);
+    return (padded - kernel) / stride + 1;
+}
+
+// Encoder tokens of a chunk of n mel frames (mel_frames_to_enc_tokens, :1300-1305).
+int enc_tokens_of(int mel) {
+    const int n = causal_conv_out_len(causal_conv_out_len(mel, 3, 1), 3, 2);
+    return n - n % kEncDownsample;
+}
+
+// Stitched token count (compute_total_enc_tokens, :1308-1325).
+int enc_tokens_total(int total_mel) {
+    const int stride_mel = kEncChunkMel - 2 * kEncChunkOverlap;
+    int total = 0;
+    for (int off = 0, first = 1; off < total_mel; off += stride_mel, first = 0) {
+        const int add = enc_tokens_of(std::min(kEncChunkMel, total_mel - off)) - (first ? 0 : kEncChunkOverlap);
+        if (add <= 0) break;
+        total += add;
+    }
+    return total;
 }
 
 // ---- conversion kernel: K/V (F32 | F16 strided | Q8_0) -> packed f16 ---------
@@ -818,6 +853,81 @@ int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int3
     if (rc != VTX_OK) return rc;
     return launch_pdl(decode_advance_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
                       static_cast<cudaStream_t>(stream), positions, slots, kv_len, (int)n, (int)window);
+}
+
+int vtx_encoder_chunk_plan(int32_t total_mel_frames, vtx_enc_chunk *chunks, int32_t max_chunks,
+                           int32_t *n_tokens_total, int32_t *n_tokens_used) {
+    if (total_mel_frames < 0 || max_chunks < 0) return VTX_ERR_SHAPE;
+    if (!chunks && max_chunks > 0) return VTX_ERR_NULL;
+    // the walk of run_encoder_chunked (src/voxtral.cpp:2234-2335)
+    const int alloc_total = enc_tokens_total(total_mel_frames);
+    const int stride_mel = kEncChunkMel - 2 * kEncChunkOverlap;
+    int n = 0, write = 0;
+    for (int off = 0; alloc_total > 0 && off < total_mel_frames; off += stride_mel) {
+        const int frames = std::min(kEncChunkMel, total_mel_frames - off);
+        const int skip = n > 0 ? kEncChunkOverlap : 0;
+        const int toks = enc_tokens_of(frames);
+        int stride = toks - skip;
+        if (stride <= 0) break;                                   // no new tokens: stop (:2265-2272, :2300-2305)
+        if (write + stride > alloc_total) {                       // clamp to the allocation (:2307-2311)
+            stride = alloc_total - write;
+            if (stride <= 0) break;
+        }
+        if (n < max_chunks) {
+            vtx_enc_chunk &c = chunks[n];
+            c.mel_offset = off; c.mel_frames = frames; c.n_tokens = toks; c.skip = skip; c.stride = stride;
+            c.rope_offset = write - skip; c.write_offset = write; c.reserved = 0;
+        }
+        write += stride;
+        ++n;
+    }
+    if (n_tokens_total) *n_tokens_total = std::max(alloc_total, 0);
+    if (n_tokens_used) *n_tokens_used = write / kEncDownsample * kEncDownsample;
+    return n;
+}
+
+int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t src_row_bytes, void *dst,
+                       size_t dst_row_bytes, size_t row_bytes, const vtx_enc_chunk *chunks, int32_t n_chunks,
+                       void *stream) {
+    if (n_chunks < 0) return VTX_ERR_SHAPE;
+    if (n_chunks == 0 || row_bytes == 0) return VTX_OK;
+    if (!src || !dst || !chunks) return VTX_ERR_NULL;
+    long long rows = 0;
+    for (int c = 0; c < n_chunks; ++c) {
+        const vtx_enc_chunk &ch = chunks[c];
+        if (ch.skip < 0 || ch.stride < 0 || ch.write_offset < 0) return VTX_ERR_SHAPE;
+        rows += ch.stride;
+    }
+    if (rows > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst) | src_chunk_bytes |
+                         src_row_bytes | dst_row_bytes | row_bytes;
+    const int vec = al % 16 == 0 ? 16 : al % 8 == 0 ? 8 : al % 4 == 0 ? 4 : 1;
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    for (int c0 = 0; c0 < n_chunks; c0 += kStitchMaxChunks) {
+        StitchArgs a{};
+        a.src = static_cast<const char *>(src); a.src_chunk = (long long)src_chunk_bytes;
+        a.src_row = (long long)src_row_bytes;
+        a.dst = static_cast<char *>(dst); a.dst_row = (long long)dst_row_bytes;
+        a.row_bytes = (long long)row_bytes;
+        a.n = std::min(kStitchMaxChunks, n_chunks - c0);
+        for (int i = 0; i < a.n; ++i) {
+            const vtx_enc_chunk &ch = chunks[c0 + i];
+            a.first[i + 1] = a.first[i] + ch.stride;
+            a.skip[i] = ch.skip; a.write[i] = ch.write_offset; a.chunk[i] = c0 + i;
+        }
+        if (a.first[a.n] == 0) continue;
+        const dim3 grid((unsigned)std::min(a.first[a.n], ds->sms * 8));
+        int r = VTX_OK;
+        if (vec == 16) r = launch_pdl(enc_stitch_kernel<16>, grid, dim3(256), 0, st, a);
+        else if (vec == 8) r = launch_pdl(enc_stitch_kernel<8>, grid, dim3(256), 0, st, a);
+        else if (vec == 4) r = launch_pdl(enc_stitch_kernel<4>, grid, dim3(256), 0, st, a);
+        else r = launch_pdl(enc_stitch_kernel<1>, grid, dim3(256), 0, st, a);
+        if (r != VTX_OK) return VTX_ERR_CUDA;
+    }
+    return VTX_OK;
 }
 
 int vtx_read_device_error(void *stream) {

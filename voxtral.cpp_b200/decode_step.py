@@ -40,6 +40,7 @@ class DecodeStepGraph:
         self.positions = start.clone().to(dev)
         self.slots = (start % window).to(torch.int32).to(dev)
         self.kv_len = torch.clamp(start + 1, max=window).to(torch.int32).to(dev)   # includes the new token
+        self._start = (self.positions.clone(), self.slots.clone(), self.kv_len.clone())
         # caches: [layer][stream] of window rows
         self.k_cache = torch.zeros((n_layers, n_seq, window, self.row), dtype=torch.uint8, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -83,6 +84,15 @@ class DecodeStepGraph:
             vtx_attn.ctypes.c_void_p(self.kv_len.data_ptr()), self.S, self.W,
             vtx_attn.ctypes.c_void_p(self.stream.cuda_stream))
         vtx_attn._check(rc, "vtx_decode_advance")
+
+    def reset(self) -> None:
+        """Rewinds every stream to its start_len (its prefill rows stay in the
+        rings): the next step writes slot start_len % window again."""
+        self.stream.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(self.stream):
+            for dst, src in zip((self.positions, self.slots, self.kv_len), self._start):
+                dst.copy_(src)
+        torch.cuda.current_stream(self.dev).wait_stream(self.stream)
 
     def step_eager(self) -> None:
         """One step issued call by call from the host (the uncaptured path)."""

@@ -71,6 +71,16 @@ class KvAppendArgs(ctypes.Structure):
                 ("cache_nb1", ctypes.c_size_t), ("reserved", ctypes.c_int32 * 4)]
 
 
+class EncChunk(ctypes.Structure):
+    """vtx_enc_chunk (include/vtx_fa.h): one chunk of the realtime encoder run."""
+    _fields_ = [("mel_offset", ctypes.c_int32), ("mel_frames", ctypes.c_int32), ("n_tokens", ctypes.c_int32),
+                ("skip", ctypes.c_int32), ("stride", ctypes.c_int32), ("rope_offset", ctypes.c_int32),
+                ("write_offset", ctypes.c_int32), ("reserved", ctypes.c_int32)]
+
+    def as_dict(self) -> dict:
+        return {f: getattr(self, f) for f, _ in self._fields_ if f != "reserved"}
+
+
 _lib = None
 
 
@@ -105,6 +115,13 @@ def load(path: str = LIB_PATH):
     L.vtx_decode_advance.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int32,
                                      ctypes.c_int32, ctypes.c_void_p]
     L.vtx_decode_advance.restype = ctypes.c_int
+    L.vtx_encoder_chunk_plan.argtypes = [ctypes.c_int32, P(EncChunk), ctypes.c_int32, P(ctypes.c_int32),
+                                         P(ctypes.c_int32)]
+    L.vtx_encoder_chunk_plan.restype = ctypes.c_int
+    L.vtx_encoder_stitch.argtypes = [ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p,
+                                     ctypes.c_size_t, ctypes.c_size_t, P(EncChunk), ctypes.c_int32,
+                                     ctypes.c_void_p]
+    L.vtx_encoder_stitch.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -279,6 +296,43 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, slots: 
     s = stream if stream is not None else torch.cuda.current_stream(k.device)
     _check(load().vtx_kv_append(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "vtx_kv_append")
     return q_out
+
+
+# ---- realtime encoder: chunk plan and device-side stitch ---------------------
+
+def encoder_chunk_plan(total_mel_frames: int):
+    """The chunks run_encoder_chunked processes for an utterance
+    (src/voxtral.cpp:2234-2335), through vtx_encoder_chunk_plan.  Returns
+    (chunks as a ctypes array of EncChunk, stitched token count, count
+    trimmed to a multiple of 4)."""
+    L = load()
+    tot, used = ctypes.c_int32(0), ctypes.c_int32(0)
+    n = L.vtx_encoder_chunk_plan(int(total_mel_frames), None, 0, ctypes.byref(tot), ctypes.byref(used))
+    _check(n if n < 0 else 0, "vtx_encoder_chunk_plan")
+    arr = (EncChunk * max(n, 1))()
+    n2 = L.vtx_encoder_chunk_plan(int(total_mel_frames), arr, n, ctypes.byref(tot), ctypes.byref(used))
+    _check(n2 if n2 < 0 else 0, "vtx_encoder_chunk_plan")
+    return (EncChunk * n).from_buffer(arr) if n else (EncChunk * 0)(), tot.value, used.value
+
+
+def encoder_stitch(chunk_out: torch.Tensor, chunks, dst: torch.Tensor,
+                   stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """Copies rows [skip, skip + stride) of each chunk's output into rows
+    [write_offset, ...) of dst on the device (vtx_encoder_stitch).
+    chunk_out: (n_chunks, rows, ...) with contiguous rows; dst: (rows_total, ...)."""
+    if chunk_out.shape[0] < len(chunks):
+        raise ValueError("fewer chunk outputs than chunks")
+    row_bytes = chunk_out[0, 0].numel() * chunk_out.element_size()
+    if dst[0].numel() * dst.element_size() != row_bytes or not chunk_out[0, 0].is_contiguous():
+        raise ValueError("row size mismatch or non-contiguous rows")
+    s = stream if stream is not None else torch.cuda.current_stream()
+    arr = (EncChunk * max(len(chunks), 1))(*chunks) if len(chunks) else (EncChunk * 1)()
+    rc = load().vtx_encoder_stitch(ctypes.c_void_p(chunk_out.data_ptr()), chunk_out.stride(0) * chunk_out.element_size(),
+                                   chunk_out.stride(1) * chunk_out.element_size(), ctypes.c_void_p(dst.data_ptr()),
+                                   dst.stride(0) * dst.element_size(), row_bytes, arr, len(chunks),
+                                   ctypes.c_void_p(s.cuda_stream))
+    _check(rc, "vtx_encoder_stitch")
+    return dst
 
 
 def read_device_error(stream: Optional[torch.cuda.Stream] = None) -> int:
