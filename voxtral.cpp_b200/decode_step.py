@@ -121,3 +121,42 @@ class DecodeStepGraph:
         with torch.cuda.stream(self.stream):
             self.graph.replay()
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+
+
+def _main() -> None:
+    """Times the replayed step of one stream: python decode_step.py [--layers L]
+    [--keys N] [--kv q8_0|f16]; prints microseconds per layer."""
+    import argparse
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--layers", type=int, default=4)
+    ap.add_argument("--keys", type=int, default=7300, help="tokens already in the ring")
+    ap.add_argument("--kv", default="q8_0", choices=["q8_0", "f16"])
+    ap.add_argument("--steps", type=int, default=20)
+    args = ap.parse_args()
+    kvt = vtx_attn.Q8_0 if args.kv == "q8_0" else vtx_attn.F16
+    L, start = args.layers, args.keys
+    g = DecodeStepGraph(L, 1, 32, 8, 128, kvt, 8192, [start], 1e6)
+    gen = torch.Generator(device=g.dev)
+    gen.manual_seed(1)
+    for l in range(L):
+        k = torch.randn((start, 8, 128), generator=gen, device=g.dev)
+        g.fill(l, 0, k, torch.randn_like(k), torch.arange(start, dtype=torch.int32))
+    g.q.normal_(generator=gen)
+    g.k.normal_(generator=gen)
+    g.v.normal_(generator=gen)
+    for _ in range(3):
+        g.step_eager()
+    g.step()                                                 # capture
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(g.stream)
+    for _ in range(args.steps):
+        g.step()
+    e1.record(g.stream)
+    torch.cuda.synchronize()
+    print(f"layers={L} keys={start} kv={args.kv}: {e0.elapsed_time(e1) / args.steps * 1e3 / L:.2f} us/layer (graph)")
+
+
+if __name__ == "__main__":
+    _main()
