@@ -217,6 +217,35 @@ def test_decode_batched_q8_0_head_groups(Hkv, G):
     assert_close(got.cpu().numpy(), ref, f"batched q8_0 decode Hkv={Hkv} G={G}")
 
 
+@pytest.mark.parametrize("kv", ["q8_0", "f16"])
+def test_decode_batched_one_stream_many_splits(kv):
+    """Batch 1 over a long ring (the decode step's shape): the key range is cut
+    into more than 32 splits, so the partials go through the 512-thread
+    combine kernel; lengths 7300 and a short 40 in a ring planned for 8192."""
+    import vtx_attn
+    rng = np.random.default_rng(55)
+    Hq, Hkv, D, W = 32, 8, 128, 8192
+    kvt = O.Q8_0 if kv == "q8_0" else O.F16
+    for L in (7300, 40):
+        qn = rng.standard_normal((1, Hq, D)).astype(np.float32)
+        kf = rng.standard_normal((W, Hkv, D)).astype(np.float32)
+        vf = rng.standard_normal((W, Hkv, D)).astype(np.float32)
+        if kv == "q8_0":
+            kb, vb = O.quantize_q8_0(kf), O.quantize_q8_0(vf)
+        else:
+            kb, vb = kf.astype(np.float16), vf.astype(np.float16)
+        lens = np.array([L], dtype=np.int32)
+        row, nb2 = kb.strides[0], kb.strides[1]
+        ref = O.decode_batched(qn, [kb[:L]], [vb[:L]], lens, 1 / np.sqrt(D), kvt, Hkv, row, nb2)
+        plan = vtx_attn.DecodeBatchPlan([torch.from_numpy(kb).cuda()], [torch.from_numpy(vb).cuda()],
+                                        torch.from_numpy(lens).cuda(), Hq, Hkv, D, kvt, row, nb2, W,
+                                        float(1 / np.sqrt(D)))
+        got = plan(torch.from_numpy(qn).cuda())
+        torch.cuda.synchronize()
+        assert vtx_attn.read_device_error() == 0
+        assert_close(got.cpu().numpy(), ref, f"one-stream {kv} decode, {L} keys in a {W}-row ring")
+
+
 # ---- error paths through the C ABI ---------------------------------------------
 
 def test_errors_are_status_codes():
