@@ -1,7 +1,7 @@
 """Benchmark of the voxtral.cpp attention node on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl vtx|reference]
-                    [--workload encoder|decode|kv_append|decode_step|realtime]
+                    [--workload encoder|decode|kv_append|decode_step|realtime|prefill]
 
 Headline workload: the Whisper-large-shaped audio
 encoder self-attention of voxtral.cpp (src/voxtral.cpp:1611): one 30 s clip ->
@@ -565,6 +565,79 @@ def run_decode_step(args, rank, world, local):
             "detail": res, "peak_hbm_gbs": peaks["hbm_gbs"], "gpu_launches": 200 * (30 * 3 + 1)}
 
 
+# ---- decoder prefill (D = 128, causal GQA) ----------------------------
+def run_prefill(args, rank, world, local):
+    """The decoder's prefill attention (src/voxtral.cpp:1802 with n_tokens =
+    n_kv and the causal mask of :2103-2111 as the causal flag), laid out as
+    the reference lays it out: Q F32 [128, n, 32] (heads contiguous per
+    token), K/V rows of the f16 cache (kv_dim 1024 per token, 8 KV heads x
+    128).  configs[2]: 391 tokens (375 audio + 16 prompt), 30 layers, each
+    layer with its own buffers, graph-replayed.  Also a long-context case
+    (8192 tokens, 4 layers) for the same kernel at full occupancy."""
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    Hq, Hkv, D = DEC["Hq"], DEC["Hkv"], DEC["D"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(515 + rank)
+    res = {}
+    for name, n, L in (("configs[2]", 391, 30), ("long_context", 8192, 4)):
+        q = torch.randn((L, n, Hq, D), generator=g, device=dev)
+        kv = torch.randn((L, 2, n, Hkv, D), generator=g, device=dev).to(torch.float16)
+        out = torch.empty((L, 1, n, Hq, D), device=dev)
+        views = [(q[l].permute(1, 0, 2).unsqueeze(0), kv[l, 0].permute(1, 0, 2).unsqueeze(0),
+                  kv[l, 1].permute(1, 0, 2).unsqueeze(0)) for l in range(L)]
+        stream = torch.cuda.Stream(device=dev)
+
+        def step():
+            for l in range(L):
+                qq, kk, vv = views[l]
+                vtx_attn.flash_attn_ext(qq, kk, vv, None, D ** -0.5, causal=True, out=out[l], stream=stream)
+
+        with torch.cuda.stream(stream):
+            step()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            step()
+        with torch.cuda.stream(stream):
+            for _ in range(max(3, args.warmup)):
+                graph.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with ClockSampler(local) as clocks:
+            barrier(world)
+            e0.record(stream)
+            with torch.cuda.stream(stream):
+                for _ in range(args.steps):
+                    graph.replay()
+            e1.record(stream)
+            torch.cuda.synchronize()
+            barrier(world)
+        ms = barrier_max(e0.elapsed_time(e1) / args.steps, world)
+        flop = 4.0 * D * Hq * (n * (n + 1) // 2) * L
+        res[name] = {"tokens": n, "layers": L, "ms_per_step": round(ms, 4),
+                     "tflops": round(flop * world / (ms * 1e-3) / 1e12, 1), "us_per_layer": round(ms * 1e3 / L, 2),
+                     "clocks": clocks.summary()}
+        del q, kv, out, graph
+        torch.cuda.empty_cache()
+    peaks = load_peaks()
+    main = res["configs[2]"]
+    return {"metric": METRIC_ENC, "value": main["tflops"], "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": main["ms_per_step"],
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic N(0,1) Q (F32) and K/V (f16), seeded per rank",
+            "config": {"workload": "configs[2] decoder prefill: 391 tokens causal, GQA 32/8 x 128, 30 layers "
+                                   "(one step = the 30 layer calls, graph-replayed)",
+                       "l2": "each layer has its own Q/K/V (8 MB per layer, 240 MB per step)",
+                       "parallelism": f"dp{world}"},
+            "roofline": {"bound": "tensor", "achieved": main["tflops"] / world, "peak": peaks["bf16_tflops"],
+                         "unit": "TFLOP/s", "frac": round(main["tflops"] / world / peaks["bf16_tflops"], 4),
+                         "traffic": None},
+            "detail": res, "gpu_launches": args.steps * 30, "clocks": main["clocks"]}
+
+
 # ---- configs[3]: realtime long-form streaming, attention path --------------------
 def run_realtime(args, rank, world, local):
     """The attention work of 10 minutes of synthetic audio through the realtime
@@ -710,7 +783,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="vtx", choices=["vtx", "reference"])
     ap.add_argument("--workload", default="encoder",
-                    choices=["encoder", "decode", "kv_append", "decode_step", "realtime"])
+                    choices=["encoder", "decode", "kv_append", "decode_step", "realtime", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
@@ -745,7 +818,7 @@ def main():
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:
         res = {"decode": run_decode, "kv_append": run_kv_append, "decode_step": run_decode_step,
-               "realtime": run_realtime}[args.workload](args, rank, world, local)
+               "realtime": run_realtime, "prefill": run_prefill}[args.workload](args, rank, world, local)
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
