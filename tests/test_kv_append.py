@@ -160,6 +160,26 @@ def test_gpu_kv_append_matches_oracle(kv_type, D):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("kv_type", [O.F16, O.Q8_0])
+def test_gpu_kv_append_many_tokens(kv_type):
+    """A prefill-sized call (400 tokens, at least two per SM): one CTA per
+    token walks all of the token's rows, where a decode step's few tokens
+    spread their rows over CTAs of 8."""
+    q, k, v, pos = make_inputs(40 + kv_type, T=400, Hq=32, Hkv=8, D=128)
+    rows = 512
+    slots = np.random.default_rng(6).permutation(rows)[:len(pos)].astype(np.int32)
+    qo, kc, vc = _gpu_append(q, k, v, pos, slots, kv_type, rows)
+    kr, vr = empty_cache(rows, 8, 128, kv_type), empty_cache(rows, 8, 128, kv_type)
+    qr = O.kv_append(q, k, v, pos, slots, kv_type, BASE, kr, vr)
+    assert_close(qo, qr, "roped Q", atol=2e-6, rtol=2e-6)
+    if kv_type == O.F16:
+        _f16_ulp_close(kc.view(np.float16), kr.view(np.float16))
+    else:
+        _q8_close(kc, kr)
+    assert np.array_equal(vc, vr)
+
+
+@pytest.mark.gpu
 def test_gpu_kv_append_per_stream_caches():
     """Batched decode: one token per stream, each into its own cache (k_cache_ptrs)."""
     import torch
