@@ -270,11 +270,55 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 if (a.window > 0) lo = max(0, tok + off - (a.window - 1));
             }
         }
-        // Q row -> f16 -> swizzled smem (K-major, 128B swizzle, 64-col sub-tiles).
-        // The whole row is loaded into registers before anything is stored: the
-        // shared-memory stores go through a generic pointer, so loads placed
-        // after them could not be hoisted and each would pay a DRAM latency.
-        {
+        // Q tile -> f16 -> swizzled smem (K-major, 128B swizzle, 64-col sub-tiles).
+        // f16 Q is copied by the warpgroup in 16-byte chunks, consecutive
+        // threads taking consecutive chunks of a row, so a warp's load touches
+        // 4 rows (D = 64) instead of 32.  F32 Q (converted) and Q quantised for
+        // a Q8_0 K are read a row per thread.  Every load is issued before any
+        // store (the stores go through a generic pointer, so a load after them
+        // could not be hoisted and would pay its own DRAM latency).
+        if (!a.q_quant8 && a.q_f16) {
+            constexpr int CPR = D / 8;                          // 16-byte f16 chunks per row
+            constexpr int PER = 128 * CPR / 128;                // chunks per thread
+            char *qtile = smem + C::Q_OFF + t * C::TILE_BYTES;
+            // addresses first; a chunk past the sequence reads the tensor's first
+            // row (always valid) and is zeroed afterwards, so the loads carry no
+            // branches and all of a thread's loads are in flight together
+            // thread r takes chunk r % CPR of rows r / CPR + i * RS; when the group
+            // size divides RS the later rows are the same head RS / G tokens on
+            // (one division per thread instead of one per chunk)
+            constexpr int RS = 128 / CPR;                       // rows per step
+            const int row0 = r / CPR, c = r % CPR;
+            const bool step_div = RS % a.G == 0;
+            const int tok0 = qt * a.tok_per_tile + row0 / a.G, head0 = g * a.G + row0 % a.G;
+            const int tstep = step_div ? RS / a.G : 0;
+            const char *src[PER];
+            bool valid[PER];
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                const int row = row0 + i * RS;
+                const int ctok = step_div ? tok0 + i * tstep : qt * a.tok_per_tile + row / a.G;
+                const int chead = step_div ? head0 : g * a.G + row % a.G;
+                valid[i] = qt < a.n_tiles_q && row < rows_per_tile && ctok < a.n_q;
+                src[i] = valid[i] ? a.q + (long long)ctok * a.q_nb1 + (long long)chead * a.q_nb2 +
+                                        (long long)b * a.q_nb3 + c * 16
+                                  : a.q;
+            }
+            uint4 pkc[PER];
+#pragma unroll
+            for (int i = 0; i < PER; ++i) pkc[i] = *reinterpret_cast<const uint4 *>(src[i]);
+#pragma unroll
+            for (int i = 0; i < PER; ++i)
+                if (!valid[i]) pkc[i] = make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+            for (int i = 0; i < PER; ++i) {
+                const int row = row0 + i * RS, sub = c >> 3, cc = c & 7;
+                *reinterpret_cast<uint4 *>(qtile + sub * 16384 + row * 128 + ((cc ^ (row & 7)) << 4)) = pkc[i];
+            }
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_full);
+        } else {
             char *qtile = smem + C::Q_OFF + t * C::TILE_BYTES;
             const char *src = a.q + (long long)tok * a.q_nb1 + (long long)head * a.q_nb2 + (long long)b * a.q_nb3;
             float f[D];
