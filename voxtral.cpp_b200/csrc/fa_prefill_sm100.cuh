@@ -22,12 +22,15 @@
 // softmax the tensor core runs the other tile's PV and next S.  The producer
 // warpgroup gives registers to the softmax warpgroups (setmaxnreg).
 //
-// TMEM columns, look-ahead layout (D = 64, or NQT = 1): per tile S_t (128),
+// TMEM columns, look-ahead layout (D = 128 with NQT = 1): per tile S_t (128),
 // P_t (64, f16 pairs), O_t (D).  The softmax releases S_t as soon as it sits
 // in registers, so S_t(j+1) = Q_t K_{j+1}^T runs during the softmax of tile
 // j and the softmax warps never wait for the tensor core in steady state.
-// Otherwise (D = 128, NQT = 2: 640 columns would be needed) P_t aliases the
-// first 64 columns of S_t and O_t sits after the S block.  Causal / windowed
+// Otherwise P_t aliases the first 64 columns of S_t and O_t sits after the S
+// block: D = 128 with NQT = 2 (640 columns would be needed), and D = 64, where
+// O_t carries 16 extra columns for the tensor-core row sum (2 x 272 > 512);
+// measured, the row sum on the tensor core is worth more than the look-ahead
+// for D = 64, whose softmax instruction stream is the bound either way.  Causal / windowed
 // key tiles outside every row's range are never loaded.  Numerics: Q and P
 // in f16 (Q is rounded to half exactly as ggml rounds Q for an F16 K), fp32
 // accumulation of S and O.
