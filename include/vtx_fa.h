@@ -49,7 +49,7 @@ extern "C" {
 #define VTX_API
 #endif
 
-#define VTX_FA_ABI_VERSION 1
+#define VTX_FA_ABI_VERSION 2
 
 /* ggml type ids (ggml/include/ggml.h enum ggml_type) */
 enum vtx_type {
@@ -131,6 +131,15 @@ VTX_API size_t vtx_flash_attn_ext_workspace(const vtx_tensor *q, const vtx_tenso
  *   v_ptrs   : same for values
  *   kv_len   : device int32 [n_seq], keys 0..kv_len[s]-1 are attended
  *   dst      : device F32 [n_seq][n_head_q][head_dim]
+ *   fresh_row: optional device int32 [n_seq]: the one key row of each stream
+ *              (index t, or -1 for none) that the kernel launched just before
+ *              this call on the stream writes, together with q -- the KV
+ *              append of the same decode step.  When given, the streaming
+ *              decode kernels start copying the other rows while that kernel
+ *              still runs (programmatic dependent launch) and wait for it only
+ *              before reading q and the fresh row; kv_len, the pointer arrays
+ *              and every other row must then be complete before that kernel.
+ *              NULL: nothing is read before the preceding kernel completes.
  * max_kv_len bounds every kv_len[s] (host-known upper bound used for sizing). */
 typedef struct vtx_decode_batch {
     int32_t n_seq;
@@ -148,6 +157,7 @@ typedef struct vtx_decode_batch {
     float              *dst;
     float   scale;
     int32_t reserved;
+    const int32_t      *fresh_row;   /* optional, see above (added in ABI version 2) */
 } vtx_decode_batch;
 
 VTX_API int vtx_flash_attn_decode_batched(const vtx_decode_batch *batch, void *workspace,

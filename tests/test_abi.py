@@ -99,7 +99,7 @@ def test_kv_append_validation_without_device(lib):
 
 
 def test_abi_version_and_strerror(lib):
-    assert lib.vtx_abi_version() == 1
+    assert lib.vtx_abi_version() == 2
     assert lib.vtx_strerror(0) == b"ok"
     assert b"workspace" in lib.vtx_strerror(-6)
 

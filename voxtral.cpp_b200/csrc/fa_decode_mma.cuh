@@ -205,7 +205,10 @@ template <int D>
 __global__ void __launch_bounds__(128, 2)
 fa_decode_mma_kernel(const SplitArgs a, int n_items)
 {
-    grid_dep_wait();
+    // With a.fresh only q and one row per stream come from the kernel launched
+    // just before: the ring fills before waiting for it (see issue() and Q).
+    const bool early = a.fresh != nullptr;
+    if (!early) grid_dep_wait();
     grid_dep_launch();
     using C = DecodeCfg<D>;
     constexpr int KC = D / 16;                      // 16-wide chunks of the head dim
@@ -248,6 +251,14 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
     __syncwarp();
     fence_mbar_init();
     __syncwarp();
+    const int fresh = early && a.k_ptrs ? a.fresh[b] : -1;   // row the preceding kernel writes
+    bool waited = !early;
+    auto dep_wait = [&]() {                          // warp-uniform
+        if (!waited) {
+            grid_dep_wait();
+            waited = true;
+        }
+    };
 
     // ---- loader: lane l copies K row l (l < 16) or V row l-16 of a stage ----
     auto issue = [&](int t) {
@@ -255,6 +266,7 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
         char *st = ring + (t % C::STAGES) * C::STAGE_BYTES;
         const int k0 = kb + t * C::KEYS;
         const int n = min(C::KEYS, ke - k0);
+        if (fresh >= k0 && fresh < k0 + n) dep_wait();   // this stage holds the fresh row
         fence_proxy_async_smem();                    // our generic reads of this stage come first
         if (lane == 0) mbar_arrive_expect_tx(&full[t % C::STAGES], (uint32_t)(2 * n * C::ROW));
         __syncwarp();
@@ -282,6 +294,7 @@ fa_decode_mma_kernel(const SplitArgs a, int n_items)
     // A fragment of m16n8k16: a0 (row l/4, col 2(l%4)), a1 (row+8), a2 (col+8), a3 (row+8, col+8)
     const int qrow = lane >> 2;
     uint32_t qa[KC][4];
+    dep_wait();                                      // q is written by the preceding kernel
     {
         const bool rq = qrow < a.G;
         const char *qp = a.q + (long long)(g * a.G + (rq ? qrow : 0)) * a.q_nb2 + (long long)b * a.q_nb3;

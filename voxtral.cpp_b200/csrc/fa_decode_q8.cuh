@@ -272,7 +272,11 @@ template <int D>
 __global__ void __launch_bounds__(DecodeQ8Cfg<D>::NTHREADS, 1)
 fa_decode_q8_kernel(const SplitArgs a, int hpc)
 {
-    grid_dep_wait();
+    // With a.fresh only q and one row per stream come from the kernel launched
+    // just before: the producer fills the ring before waiting for it, except
+    // for the stage holding that row; the head warps wait before reading q.
+    const bool early = a.fresh != nullptr;
+    if (!early) grid_dep_wait();
     grid_dep_launch();
     using C = DecodeQ8Cfg<D>;
     constexpr int NBLK = C::NBLK, NJ = D / 16;
@@ -327,6 +331,8 @@ fa_decode_q8_kernel(const SplitArgs a, int hpc)
     constexpr int HEAD_WARPS = C::HPC_MAX * C::WPH;
     if (warp == HEAD_WARPS) {
         // ================= producer =========================================
+        const int fresh = early && a.k_ptrs ? a.fresh[b] : -1;   // row the preceding kernel writes
+        bool waited = !early;
         int issued = 0;
         for (int t = 0; t < ntiles; ++t) {
             const int stg = t % C::STAGES;
@@ -335,6 +341,10 @@ fa_decode_q8_kernel(const SplitArgs a, int hpc)
                 break;
             const int k0 = kb + t * C::KEYS;
             const int n = min(C::KEYS, ke - k0);
+            if (!waited && fresh >= k0 && fresh < k0 + n) {   // this stage holds the fresh row
+                grid_dep_wait();
+                waited = true;
+            }
             char *st = smem + stg * C::RING_STAGE;
             if (lane == 0) mbar_arrive_expect_tx(&full[stg], (uint32_t)(2 * n * trow));
             __syncwarp();
@@ -373,6 +383,7 @@ fa_decode_q8_kernel(const SplitArgs a, int hpc)
     const int qr = lane >> 2, qc = lane & 3;
     uint32_t qb[NBLK][2];
     float dq[NBLK][2];
+    if (early) grid_dep_wait();                              // q is written by the preceding kernel
     {
         const bool rq = qr < a.G;
         const char *qp = a.q + (long long)(g * a.G + (rq ? qr : 0)) * a.q_nb2 + (long long)b * a.q_nb3;

@@ -41,6 +41,10 @@ struct SplitArgs {
     int write_final;
     int vec;                                   // cp.async width: 16, 8 or 4 bytes
     int *err;                                  // device error word (misaligned stream base)
+    // batched decode: per stream the row written by the kernel just before
+    // (-1: none); when set the streaming decode kernels read every other row
+    // before waiting for that kernel (programmatic dependent launch)
+    const int *fresh;
 };
 
 template <int KVT> struct KvTraits;

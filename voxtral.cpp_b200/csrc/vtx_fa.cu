@@ -765,7 +765,7 @@ int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, si
     SplitArgs a{};
     a.q = reinterpret_cast<const char *>(b->q);
     a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
-    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len;
+    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len; a.fresh = b->fresh_row;
     a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
     a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
     a.k_bdiv = a.v_bdiv = 1;
@@ -1010,7 +1010,7 @@ extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, 
     SplitArgs a{};
     a.q = reinterpret_cast<const char *>(b->q);
     a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
-    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len;
+    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len; a.fresh = b->fresh_row;
     a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
     a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
     a.k_bdiv = a.v_bdiv = 1;

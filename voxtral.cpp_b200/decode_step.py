@@ -58,7 +58,8 @@ class DecodeStepGraph:
         for l in range(n_layers):
             p = vtx_attn.DecodeBatchPlan([self.k_cache[l, s] for s in range(n_seq)],
                                          [self.v_cache[l, s] for s in range(n_seq)], self.kv_len, n_head_q,
-                                         n_head_kv, head_dim, kv_type, self.row, hb, window, head_dim ** -0.5)
+                                         n_head_kv, head_dim, kv_type, self.row, hb, window, head_dim ** -0.5,
+                                         fresh_row=self.slots)      # the append just before writes this row
             self.plans.append(p)
         self.stream = torch.cuda.Stream(device=dev)
         self.graph: Optional[torch.cuda.CUDAGraph] = None

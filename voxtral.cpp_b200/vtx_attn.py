@@ -53,7 +53,7 @@ class DecodeBatch(ctypes.Structure):
                 ("q", ctypes.c_void_p), ("k_ptrs", ctypes.c_void_p),
                 ("v_ptrs", ctypes.c_void_p), ("kv_len", ctypes.c_void_p),
                 ("dst", ctypes.c_void_p), ("scale", ctypes.c_float),
-                ("reserved", ctypes.c_int32)]
+                ("reserved", ctypes.c_int32), ("fresh_row", ctypes.c_void_p)]
 
 
 class KvAppendArgs(ctypes.Structure):
@@ -230,7 +230,10 @@ class DecodeBatchPlan:
 
     def __init__(self, k_bufs: Sequence[torch.Tensor], v_bufs: Sequence[torch.Tensor],
                  kv_len: torch.Tensor, n_head_q: int, n_head_kv: int, head_dim: int, kv_type: int,
-                 kv_nb1: int, kv_nb2: int, max_kv_len: int, scale: float):
+                 kv_nb1: int, kv_nb2: int, max_kv_len: int, scale: float,
+                 fresh_row: Optional[torch.Tensor] = None):
+        """fresh_row: optional device int32 [n_seq], the row of each stream that
+        the kernel launched just before each call writes (vtx_decode_batch)."""
         dev = kv_len.device
         self.k_ptrs = torch.tensor([t.data_ptr() for t in k_bufs], dtype=torch.int64, device=dev)
         self.v_ptrs = torch.tensor([t.data_ptr() for t in v_bufs], dtype=torch.int64, device=dev)
@@ -241,6 +244,8 @@ class DecodeBatchPlan:
         b.kv_type, b.max_kv_len, b.kv_nb1, b.kv_nb2 = kv_type, max_kv_len, kv_nb1, kv_nb2
         b.k_ptrs, b.v_ptrs, b.kv_len = self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(), self.kv_len.data_ptr()
         b.scale = scale
+        self.fresh_row = fresh_row
+        b.fresh_row = fresh_row.data_ptr() if fresh_row is not None else None
         self.batch = b
         need = load().vtx_flash_attn_decode_batched_workspace(ctypes.byref(b))
         if need == ctypes.c_size_t(-1).value:
