@@ -246,6 +246,37 @@ def test_decode_batched_one_stream_many_splits(kv):
         assert_close(got.cpu().numpy(), ref, f"one-stream {kv} decode, {L} keys in a {W}-row ring")
 
 
+@pytest.mark.parametrize("kv", ["f16", "q8_0"])
+def test_decode_batched_empty_streams(kv):
+    """Streams with no keys yet (kv_len 0) among ragged ones: their rows come
+    out zero, as ggml's S = 0 gives, and the others are unaffected."""
+    import vtx_attn
+    rng = np.random.default_rng(77)
+    Hq, Hkv, D = 32, 8, 128
+    kvt = O.Q8_0 if kv == "q8_0" else O.F16
+    lens = np.array([0, 5, 0, 1300, 0], dtype=np.int32)
+    qn = rng.standard_normal((len(lens), Hq, D)).astype(np.float32)
+    ks, vs = [], []
+    for L in lens:
+        kf = rng.standard_normal((max(int(L), 1), Hkv, D)).astype(np.float32)
+        vf = rng.standard_normal((max(int(L), 1), Hkv, D)).astype(np.float32)
+        if kv == "q8_0":
+            ks.append(O.quantize_q8_0(kf)); vs.append(O.quantize_q8_0(vf))
+        else:
+            ks.append(kf.astype(np.float16)); vs.append(vf.astype(np.float16))
+    row, nb2 = ks[0].strides[0], ks[0].strides[1]
+    ref = O.decode_batched(qn, ks, vs, lens, 1 / np.sqrt(D), kvt, Hkv, row, nb2)
+    plan = vtx_attn.DecodeBatchPlan([torch.from_numpy(a).cuda() for a in ks], [torch.from_numpy(a).cuda() for a in vs],
+                                    torch.from_numpy(lens).cuda(), Hq, Hkv, D, kvt, row, nb2, int(lens.max()),
+                                    float(1 / np.sqrt(D)))
+    got = plan(torch.from_numpy(qn).cuda())
+    torch.cuda.synchronize()
+    assert vtx_attn.read_device_error() == 0
+    got = got.cpu().numpy()
+    assert not got[lens == 0].any()
+    assert_close(got, ref, f"batched {kv} decode with empty streams")
+
+
 # ---- error paths through the C ABI ---------------------------------------------
 
 def test_errors_are_status_codes():
