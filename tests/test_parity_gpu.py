@@ -101,6 +101,20 @@ def test_q8_0_prefill():
     check(make_case(9, Hq=8, Hkv=2, n_q=150, n_kv=300, D=128, kv="q8_0", causal=1), "q8_0 prefill")
 
 
+# ---- causal launches of more than one wave (longest-first CTA order) ----------
+
+def test_realtime_encoder_chunk_multi_wave():
+    """The realtime encoder's chunk (1500 tokens, 32 heads x 64, causal +
+    window 750): 192 CTAs, more than one wave, so the CTAs run longest first."""
+    check(make_case(12, Hq=32, Hkv=32, n_q=1500, n_kv=1500, D=64, causal=1, window=750, cache=False),
+          "realtime encoder chunk")
+
+
+def test_decoder_prefill_multi_wave():
+    """A longer decoder prefill (1200 tokens, GQA 32/8 x 128, causal): 152 CTAs."""
+    check(make_case(13, Hq=32, Hkv=8, n_q=1200, n_kv=1200, D=128, causal=1, n_ctx=8192), "prefill 1200 tokens")
+
+
 # ---- edge cases --------------------------------------------------------------
 
 @pytest.mark.parametrize("n", [1, 2, 31, 33, 127, 129, 257])

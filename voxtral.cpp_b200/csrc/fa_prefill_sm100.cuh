@@ -60,6 +60,7 @@ struct PrefillArgs {
     int q_quant8;             // K was Q8_0: quantize Q rows like ggml's from_float
     int o_tma;                // dst written by TMA stores through tmO (aligned F32 dst)
     int *err;
+    int lpt;                  // launch the LPT instantiation (longest Q-tile groups first)
 };
 
 template <int D, int NQT> struct PrefillCfg {
@@ -176,7 +177,7 @@ __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.
 // non-positive scale (logits formed before the exponent); a template flag so
 // the common instantiation carries none of that code (the softmax loop is
 // fully unrolled, and its size is what the instruction cache sees).
-template <int D, int NQT, bool HAS_MASK, bool UNFUSED>
+template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool LPT = false>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO, const PrefillArgs a)
@@ -196,8 +197,15 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int g = blockIdx.y, b = blockIdx.z;
-    const int qt0 = blockIdx.x * NQT;
+    // CTA -> (KV head g, group of NQT Q tiles).  Grid (groups, Hkv, B), a
+    // head's CTAs adjacent; with LPT (a causal launch of more than one wave,
+    // whose key ranges grow with the group) grid (groups x Hkv, 1, B) taken
+    // group-major from the last group, so every head's longest CTAs are
+    // dispatched first and the short ones fill the tail (longest-first list
+    // scheduling).
+    const int b = blockIdx.z;
+    const int g = LPT ? (int)(blockIdx.x % a.Hkv) : (int)blockIdx.y;
+    const int qt0 = (LPT ? a.n_cta_q - 1 - (int)(blockIdx.x / a.Hkv) : (int)blockIdx.x) * NQT;
     const int rows_per_tile = a.tok_per_tile * a.G;
     const int off = a.n_kv - a.n_q;
 
