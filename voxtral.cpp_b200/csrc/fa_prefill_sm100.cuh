@@ -60,7 +60,7 @@ struct PrefillArgs {
     int q_quant8;             // K was Q8_0: quantize Q rows like ggml's from_float
     int o_tma;                // dst written by TMA stores through tmO (aligned F32 dst)
     int *err;
-    int lpt;                  // launch the LPT instantiation (longest Q-tile groups first)
+    int lpt;                  // causal launches: longest Q-tile groups first (see the kernel)
 };
 
 template <int D, int NQT> struct PrefillCfg {
@@ -177,7 +177,7 @@ __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.
 // non-positive scale (logits formed before the exponent); a template flag so
 // the common instantiation carries none of that code (the softmax loop is
 // fully unrolled, and its size is what the instruction cache sees).
-template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool LPT = false>
+template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool CSL = false>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO, const PrefillArgs a)
@@ -197,15 +197,21 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // CTA -> (KV head g, group of NQT Q tiles).  Grid (groups, Hkv, B), a
-    // head's CTAs adjacent; with LPT (a causal launch of more than one wave,
-    // whose key ranges grow with the group) grid (groups x Hkv, 1, B) taken
-    // group-major from the last group, so every head's longest CTAs are
-    // dispatched first and the short ones fill the tail (longest-first list
-    // scheduling).
+    // CSL: the instantiation for causal launches with the causal/window flags
+    // (no mask tensor, no softcap) that are windowed or more than one wave
+    // (measured: a single-wave plain causal launch gains nothing from it).
+    // Its CTAs' key ranges grow with their Q tiles, and it differs in two ways:
+    //   * a.lpt (more than one wave): grid (groups x Hkv, 1, B) taken
+    //     group-major from the last group of Q tiles, so every head's longest
+    //     CTAs are dispatched first and the short ones fill the tail
+    //     (longest-first list scheduling); otherwise, as for every other
+    //     launch, grid (groups, Hkv, B) with a head's CTAs adjacent;
+    //   * each Q tile runs only over its own key tiles (tile_iters below),
+    //     not over the union of the CTA's tiles.
     const int b = blockIdx.z;
-    const int g = LPT ? (int)(blockIdx.x % a.Hkv) : (int)blockIdx.y;
-    const int qt0 = (LPT ? a.n_cta_q - 1 - (int)(blockIdx.x / a.Hkv) : (int)blockIdx.x) * NQT;
+    const bool lpt = CSL && a.lpt;
+    const int g = lpt ? (int)(blockIdx.x % a.Hkv) : (int)blockIdx.y;
+    const int qt0 = (lpt ? a.n_cta_q - 1 - (int)(blockIdx.x / a.Hkv) : (int)blockIdx.x) * NQT;
     const int rows_per_tile = a.tok_per_tile * a.G;
     const int off = a.n_kv - a.n_q;
 
@@ -220,6 +226,28 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     const int j_begin = kv_lo / C::BN;
     const int j_end = kv_hi >= kv_lo ? kv_hi / C::BN + 1 : j_begin;
     const int n_iter = j_end - j_begin;
+    // Q tile t iterates over it in [lo_it, hi_it) of the CTA's key tiles.
+    // CSL: a tile's own range -- in a window or causal pair the first tile
+    // needs none of the union's last key tile (wholly in its future) and the
+    // second none of its first (wholly before its window).  A tile past the
+    // sequence has none.  Other launches: the whole range.
+    auto tile_iters = [&](int t, int &lo_it, int &hi_it) {
+        lo_it = 0;
+        hi_it = n_iter;
+        if constexpr (CSL) {
+            const int qt = qt0 + t;
+            const int tf = qt * a.tok_per_tile;
+            const int tl = min(a.n_q - 1, (qt + 1) * a.tok_per_tile - 1);
+            const int lo = a.window > 0 ? max(0, tf + off - (a.window - 1)) : 0;
+            const int hi = min(a.n_kv - 1, tl + off);
+            if (qt >= a.n_tiles_q || tf > tl || hi < lo) {
+                hi_it = 0;
+            } else {
+                lo_it = max(0, lo / C::BN - j_begin);
+                hi_it = min(n_iter, hi / C::BN + 1 - j_begin);
+            }
+        }
+    };
 
     if (tid == 0) {
         mbar_init(q_full, 4 * NQT);               // one arrival per softmax warp
@@ -403,9 +431,12 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         const float cx = a.cx;
         float m_run = -INFINITY, l_run = 0.0f;
 
-        for (int it = 0; it < n_iter && ok; ++it) {
+        int t_lo, t_hi;
+        tile_iters(t, t_lo, t_hi);
+        const int t_iters = t_hi - t_lo;
+        for (int it = t_lo; it < t_hi && ok; ++it) {
             const int j = j_begin + it;
-            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], it & 1, a.err, VTX_KERR_S));
+            ok = __all_sync(0xffffffffu, mbar_wait(&s_full[t], (it - t_lo) & 1, a.err, VTX_KERR_S));
             if (!ok) break;
             tc_fence_after();
             float s[128];
@@ -459,7 +490,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (mx > m_run + 8.0f) {                 // lazy rescale: only on a 2^8 jump
                 if (m_run != -INFINITY) {
                     alpha = ex2(m_run - mx);
-                    rescale = it > 0;
+                    rescale = it > t_lo;
                 }
                 m_run = mx;
                 l_run *= alpha;
@@ -493,8 +524,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             uint32_t pk[64];
 #pragma unroll
             for (int i = 0; i < 64; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
-            if (C::LA && it > 0) {                  // P_t and O_t are free once the previous P V retired
-                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (it - 1) & 1, a.err, VTX_KERR_O));
+            if (C::LA && it > t_lo) {               // P_t and O_t are free once the previous P V retired
+                ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (it - t_lo - 1) & 1, a.err, VTX_KERR_O));
                 if (!ok) break;
                 tc_fence_after();
             }
@@ -538,7 +569,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (ok) {
                 tc_fence_after();
                 if constexpr (C::ROWSUM) {
-                    if (n_iter > 0) {
+                    if (t_iters > 0) {
                         l_run = __uint_as_float(tmem_ld1(o_addr + D));
                         tmem_ld_wait();
                     }
@@ -547,7 +578,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
-                    if (n_iter > 0) {
+                    if (t_iters > 0) {
                         tmem_ld32(o_addr + c * 32, o);
                         tmem_ld_wait();
                     } else {
@@ -580,7 +611,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (ok) {
                 tc_fence_after();
                 if constexpr (C::ROWSUM) {
-                    if (n_iter > 0) {
+                    if (t_iters > 0) {
                         l_run = __uint_as_float(tmem_ld1(o_addr + D));
                         tmem_ld_wait();
                     }
@@ -589,7 +620,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
 #pragma unroll
                 for (int c = 0; c < D / 32; ++c) {
                     uint32_t o[32];
-                    if (n_iter > 0) {
+                    if (t_iters > 0) {
                         tmem_ld32(o_addr + c * 32, o);
                         tmem_ld_wait();
                     } else {
@@ -754,15 +785,18 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     tc_fence_after();
 #pragma unroll
                     for (int t = 0; t < NQT; ++t) {
-                        if (it > 0) {
-                            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], (it - 1) & 1, a.err, VTX_KERR_P))) {
+                        int t_lo, t_hi;
+                        tile_iters(t, t_lo, t_hi);
+                        const int pi = it - 1;                 // the key tile whose P V is due
+                        if (pi >= t_lo && pi < t_hi) {
+                            if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], (pi - t_lo) & 1, a.err, VTX_KERR_P))) {
                                 good = false;
                                 break;
                             }
                             tc_fence_after();
-                            issue_pv(t, pst, it > 1 ? 1u : 0u);
+                            issue_pv(t, pst, pi > t_lo ? 1u : 0u);
                         }
-                        if (it < n_iter) issue_qk(t, st);
+                        if (it >= t_lo && it < t_hi) issue_qk(t, st);
                     }
                     if (!good) break;
                     if (it > 0) mma_commit_w(lead, &kv_empty[pst]);

@@ -527,7 +527,7 @@ bool batch_streaming(const vtx_decode_batch *b) {
     return b->kv_type == VTX_TYPE_F16 && vec == 16;
 }
 
-template <int D, int NQT, bool HM, bool UF, bool LPT = false>
+template <int D, int NQT, bool HM, bool UF, bool CSL = false>
 int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const PrefillArgs &a,
                      dim3 grid, cudaStream_t st) {
     using C = PrefillCfg<D, NQT>;
@@ -535,19 +535,21 @@ int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtenso
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM, UF, LPT>,
+        if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return VTX_ERR_CUDA;
         attr_done[dev] = 1;
     }
-    return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, LPT>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo,
+    return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo,
                       a);
 }
 
 template <int D, int NQT>
 int launch_prefill_d(bool hm, bool uf, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
                      const PrefillArgs &a, dim3 grid, cudaStream_t st) {
-    if (a.lpt) return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, a, grid, st);   // causal, flags only
+    // windowed or multi-wave causal launches (flags only): the causal instantiation
+    if (a.causal && !hm && !uf && (a.lpt || a.window > 0))
+        return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, a, grid, st);
     if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, mo, a, grid, st)
                       : launch_prefill_t<D, NQT, false, true>(mk, mv, mo, a, grid, st);
     return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, mo, a, grid, st)
@@ -681,8 +683,9 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         a.o_tma = encode_out_map(&mo, dst->data, g.D, g.Hq, g.n_q, g.B, dst->nb[1], dst->nb[2], dst->nb[3], g.G,
                                  pp.tok_per_tile) == VTX_OK;
         if ((long long)pp.n_cta_q * g.Hkv > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
-        // more than one wave of a causal launch without a mask tensor or softcap:
-        // the longest-first instantiation (see the kernel)
+        // causal launches without a mask tensor or softcap, windowed or of more
+        // than one wave, run the causal instantiation; beyond one wave its CTAs
+        // go longest first (see the kernel)
         a.lpt = params->causal && !mask && a.fused && (long long)pp.n_cta_q * g.Hkv * g.B > ds->sms;
         const dim3 grid = a.lpt ? dim3((unsigned)(pp.n_cta_q * g.Hkv), 1, g.B) : dim3(pp.n_cta_q, g.Hkv, g.B);
         return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, mo, a, grid, st);
