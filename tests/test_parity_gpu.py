@@ -110,6 +110,14 @@ def test_realtime_encoder_chunk_multi_wave():
           "realtime encoder chunk")
 
 
+def test_encoder_chunk_window_single_wave():
+    """The window-750 chunk with 20 heads: 120 CTAs of two Q tiles, one wave,
+    so the causal instantiation keeps the head-major grid while each tile of
+    a pair runs over its own key tiles."""
+    check(make_case(14, Hq=20, Hkv=20, n_q=1500, n_kv=1500, D=64, causal=1, window=750, cache=False),
+          "encoder chunk, 20 heads")
+
+
 def test_decoder_prefill_multi_wave():
     """A longer decoder prefill (1200 tokens, GQA 32/8 x 128, causal): 152 CTAs."""
     check(make_case(13, Hq=32, Hkv=8, n_q=1200, n_kv=1200, D=128, causal=1, n_ctx=8192), "prefill 1200 tokens")
