@@ -61,6 +61,7 @@ struct PrefillArgs {
     int o_tma;                // dst written by TMA stores through tmO (aligned F32 dst)
     int *err;
     int lpt;                  // causal launches: longest Q-tile groups first (see the kernel)
+    int q_tma;                // f16 Q tiles loaded by TMA through tmQ (else copied by the softmax warps)
 };
 
 template <int D, int NQT> struct PrefillCfg {
@@ -180,7 +181,8 @@ __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.
 template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool CSL = false>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
-                        const __grid_constant__ CUtensorMap tmO, const PrefillArgs a)
+                        const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmQ,
+                        const PrefillArgs a)
 {
     using C = PrefillCfg<D, NQT>;
     extern __shared__ __align__(1024) char smem_raw[];
@@ -250,7 +252,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     };
 
     if (tid == 0) {
-        mbar_init(q_full, 4 * NQT);               // one arrival per softmax warp
+        mbar_init(q_full, a.q_tma ? 1 : 4 * NQT);   // the TMA thread, or one arrival per softmax warp
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
@@ -271,6 +273,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     if (warp == C::TMA_WARP && lane == 0) {
         tma_prefetch_desc(&tmK);
         tma_prefetch_desc(&tmV);
+        if (a.q_tma) tma_prefetch_desc(&tmQ);
     }
     grid_dep_wait();            // barriers, TMEM and the constant block above overlap the previous kernel
     grid_dep_launch();
@@ -316,7 +319,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         // a Q8_0 K are read a row per thread.  Every load is issued before any
         // store (the stores go through a generic pointer, so a load after them
         // could not be hoisted and would pay its own DRAM latency).
-        if (!a.q_quant8 && a.q_f16) {
+        if (a.q_tma) {
+            // the TMA producer loads this tile (rows past the sequence read as zeros)
+        } else if (!a.q_quant8 && a.q_f16) {
             constexpr int CPR = D / 8;                          // 16-byte f16 chunks per row
             constexpr int PER = 128 * CPR / 128;                // chunks per thread
             char *qtile = smem + C::Q_OFF + t * C::TILE_BYTES;
@@ -666,6 +671,17 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             // =================== TMA producer =================================
             if (lane == 0) {
                 const int bkv = b / a.kv_bdiv;
+                if (a.q_tma) {
+                    // the Q tiles first: box = 64 columns x G heads x tok_per_tile
+                    // tokens, i.e. the tile's 128 rows (token * G + head)
+                    mbar_arrive_expect_tx(q_full, NQT * C::TILE_BYTES);
+#pragma unroll
+                    for (int t = 0; t < NQT; ++t)
+#pragma unroll
+                        for (int sub = 0; sub < C::SUB; ++sub)
+                            tma_load_4d(smem + C::Q_OFF + t * C::TILE_BYTES + sub * 16384, &tmQ, q_full, sub * 64,
+                                        g * a.G, (qt0 + t) * a.tok_per_tile, b);
+                }
                 int issued = 0;
                 for (int it = 0; it < n_iter; ++it) {
                     const int st = it % C::STAGES;

@@ -344,6 +344,30 @@ int encode_kv_map(CUtensorMap *m, const void *ptr, int D, int n_kv, int H, int B
     return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
 }
 
+// Q map for the prefill's TMA loads: f16 [D, Hq, n_q, B] (ggml's q strides
+// nb2 = head, nb1 = token, nb3 = batch) with boxes of 64 columns x G heads x
+// tok_per_tile tokens: one 128-row Q tile, rows token * G + head, in the
+// 128-byte swizzle of the K tiles.  VTX_ERR_STRIDE when Q cannot be described
+// (the softmax warps then copy Q themselves).
+int encode_q_map(CUtensorMap *m, const void *ptr, int D, int Hq, int n_q, int B, size_t nb1, size_t nb2, size_t nb3,
+                 int G, int tok_per_tile) {
+    if (!g_encode) return VTX_ERR_CUDA;
+    if (reinterpret_cast<uintptr_t>(ptr) % 16 || G * tok_per_tile != 128) return VTX_ERR_STRIDE;
+    const size_t s1 = Hq > 1 ? nb2 : (size_t)D * 2;          // extent-1 dimensions: any legal stride
+    const size_t s2 = n_q > 1 ? nb1 : s1 * (size_t)Hq;
+    const size_t s3 = B > 1 ? nb3 : s2 * (size_t)n_q;
+    cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hq, (cuuint64_t)n_q, (cuuint64_t)B};
+    cuuint64_t strides[3] = {(cuuint64_t)s1, (cuuint64_t)s2, (cuuint64_t)s3};
+    for (int i = 0; i < 3; ++i)
+        if (strides[i] % 16 || strides[i] == 0 || strides[i] >= (1ULL << 40)) return VTX_ERR_STRIDE;
+    cuuint32_t box[4] = {64, (cuuint32_t)G, (cuuint32_t)tok_per_tile, 1};
+    cuuint32_t estr[4] = {1, 1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void *>(ptr), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
+}
+
 // Output map for the prefill epilogue's TMA stores: F32 [D, Hq, n_q, B] with
 // boxes of 32 columns x G heads x tok_per_tile tokens (one 128-row Q tile).
 // Returns VTX_ERR_STRIDE when the destination cannot be described (base or
@@ -528,8 +552,8 @@ bool batch_streaming(const vtx_decode_batch *b) {
 }
 
 template <int D, int NQT, bool HM, bool UF, bool CSL = false>
-int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const PrefillArgs &a,
-                     dim3 grid, cudaStream_t st) {
+int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const CUtensorMap &mq,
+                     const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     using C = PrefillCfg<D, NQT>;
     static int attr_done[kMaxDevices] = {0};
     int dev = 0;
@@ -541,29 +565,29 @@ int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtenso
         attr_done[dev] = 1;
     }
     return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo,
-                      a);
+                      mq, a);
 }
 
 template <int D, int NQT>
 int launch_prefill_d(bool hm, bool uf, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
-                     const PrefillArgs &a, dim3 grid, cudaStream_t st) {
+                     const CUtensorMap &mq, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     // windowed or multi-wave causal launches (flags only): the causal instantiation
     if (a.causal && !hm && !uf && (a.lpt || a.window > 0))
-        return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, a, grid, st);
-    if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, mo, a, grid, st)
-                      : launch_prefill_t<D, NQT, false, true>(mk, mv, mo, a, grid, st);
-    return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, mo, a, grid, st)
-              : launch_prefill_t<D, NQT, false, false>(mk, mv, mo, a, grid, st);
+        return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, mq, a, grid, st);
+    if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, mo, mq, a, grid, st)
+                      : launch_prefill_t<D, NQT, false, true>(mk, mv, mo, mq, a, grid, st);
+    return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, mo, mq, a, grid, st)
+              : launch_prefill_t<D, NQT, false, false>(mk, mv, mo, mq, a, grid, st);
 }
 
 int launch_prefill(int D, int nqt, bool hm, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
-                   const PrefillArgs &a, dim3 grid, cudaStream_t st) {
+                   const CUtensorMap &mq, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     const bool uf = !a.fused;
     if (D == 64)
-        return nqt == 2 ? launch_prefill_d<64, 2>(hm, uf, mk, mv, mo, a, grid, st)
-                        : launch_prefill_d<64, 1>(hm, uf, mk, mv, mo, a, grid, st);
-    return nqt == 2 ? launch_prefill_d<128, 2>(hm, uf, mk, mv, mo, a, grid, st)
-                    : launch_prefill_d<128, 1>(hm, uf, mk, mv, mo, a, grid, st);
+        return nqt == 2 ? launch_prefill_d<64, 2>(hm, uf, mk, mv, mo, mq, a, grid, st)
+                        : launch_prefill_d<64, 1>(hm, uf, mk, mv, mo, mq, a, grid, st);
+    return nqt == 2 ? launch_prefill_d<128, 2>(hm, uf, mk, mv, mo, mq, a, grid, st)
+                    : launch_prefill_d<128, 1>(hm, uf, mk, mv, mo, mq, a, grid, st);
 }
 
 size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, int sms) {
@@ -682,13 +706,18 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         std::memset(&mo, 0, sizeof(mo));
         a.o_tma = encode_out_map(&mo, dst->data, g.D, g.Hq, g.n_q, g.B, dst->nb[1], dst->nb[2], dst->nb[3], g.G,
                                  pp.tok_per_tile) == VTX_OK;
+        CUtensorMap mq;
+        std::memset(&mq, 0, sizeof(mq));
+        a.q_tma = q->type == VTX_TYPE_F16 && !a.q_quant8 &&
+                  encode_q_map(&mq, q->data, g.D, g.Hq, g.n_q, g.B, q->nb[1], q->nb[2], q->nb[3], g.G,
+                               pp.tok_per_tile) == VTX_OK;
         if ((long long)pp.n_cta_q * g.Hkv > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
         // causal launches without a mask tensor or softcap, windowed or of more
         // than one wave, run the causal instantiation; beyond one wave its CTAs
         // go longest first (see the kernel)
         a.lpt = params->causal && !mask && a.fused && (long long)pp.n_cta_q * g.Hkv * g.B > ds->sms;
         const dim3 grid = a.lpt ? dim3((unsigned)(pp.n_cta_q * g.Hkv), 1, g.B) : dim3(pp.n_cta_q, g.Hkv, g.B);
-        return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, mo, a, grid, st);
+        return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, mo, mq, a, grid, st);
     }
 
     // ---- split-KV path ---------------------------------------------------------
