@@ -13,8 +13,10 @@
 //                   columns, a degree-3 polynomial on the FMA pipe for the
 //                   rest), lazy rescaling (only when the row max grows by more
 //                   than 2^8), P packed to half into its TMEM columns.
-//   WG NQT warp 0   TMA producer: K_j, V_j (128 keys x D, 128-byte swizzle)
-//                   into a STAGES-deep shared-memory ring (mbarrier tx count)
+//   WG NQT warp 0   TMA producer: the f16 Q tiles first (when Q is
+//                   TMA-describable), then K_j, V_j (128 keys x D, 128-byte
+//                   swizzle) into a STAGES-deep shared-memory ring (mbarrier
+//                   tx count)
 //   WG NQT warp 1   MMA issuer (one thread): S_t = Q_t K_j^T  (SS, f16->f32,
 //                   TMEM), then O_t += P_t V_j with P read from TMEM (TS)
 //
@@ -313,7 +315,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             }
         }
         // Q tile -> f16 -> swizzled smem (K-major, 128B swizzle, 64-col sub-tiles).
-        // f16 Q is copied by the warpgroup in 16-byte chunks, consecutive
+        // f16 Q that a tensor map describes arrives by TMA (a.q_tma, issued by
+        // the producer ahead of the K/V stages).  Other f16 Q is copied by the
+        // warpgroup in 16-byte chunks, consecutive
         // threads taking consecutive chunks of a row, so a warp's load touches
         // 4 rows (D = 64) instead of 32.  F32 Q (converted) and Q quantised for
         // a Q8_0 K are read a row per thread.  Every load is issued before any
