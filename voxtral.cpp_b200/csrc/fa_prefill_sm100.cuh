@@ -575,6 +575,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             // the hardware.
             static_assert(NQT * (D / 32) * 16384 <= C::BAR_OFF, "O staging overlaps the barriers");
             char *st = smem + C::Q_OFF + t * (D / 32) * 16384;
+            float inv = 0.0f;
             if (ok) {
                 tc_fence_after();
                 if constexpr (C::ROWSUM) {
@@ -583,9 +584,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                         tmem_ld_wait();
                     }
                 }
-                const float inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
+                inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
+            }
+            const bool store = __all_sync(0xffffffffu, ok) && r == 0 && qt < a.n_tiles_q;
+            // one box at a time: its store is issued as soon as it is staged, so
+            // the TMA reads box c while the warpgroup stages box c + 1
 #pragma unroll
-                for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < D / 32; ++c) {
+                if (ok) {
                     uint32_t o[32];
                     if (t_iters > 0) {
                         tmem_ld32(o_addr + c * 32, o);
@@ -600,16 +606,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                             make_float4(__uint_as_float(o[4 * q4]) * inv, __uint_as_float(o[4 * q4 + 1]) * inv,
                                         __uint_as_float(o[4 * q4 + 2]) * inv, __uint_as_float(o[4 * q4 + 3]) * inv);
                 }
-            }
-            fence_proxy_async_smem();
-            asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // this tile's rows are staged
-            if (__all_sync(0xffffffffu, ok) && r == 0 && qt < a.n_tiles_q) {
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c)
+                fence_proxy_async_smem();
+                asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // box c of this tile is staged
+                if (store) {
                     tma_store_4d(&tmO, st + c * 16384, c * 32, g * a.G, qt * a.tok_per_tile, b);
-                bulk_commit();
-                bulk_wait_read_all();   // shared memory must stay valid until the stores have read it
+                    bulk_commit();
+                }
             }
+            if (store) bulk_wait_read_all();   // shared memory must stay valid until the stores have read it
         } else {
             // O rows are staged in the (now idle) Q tiles + K/V ring, padded by
             // 16 B per row, then written back as whole rows with 16 B per lane
