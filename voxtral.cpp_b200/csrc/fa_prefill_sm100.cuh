@@ -15,8 +15,8 @@
 //                   than 2^8), P packed to half into its TMEM columns.
 //   WG NQT warp 0   TMA producer: the f16 Q tiles first (when Q is
 //                   TMA-describable), then K_j, V_j (128 keys x D, 128-byte
-//                   swizzle) into a STAGES-deep shared-memory ring (mbarrier
-//                   tx count)
+//                   swizzle) into a STAGES-deep shared-memory ring (one
+//                   mbarrier tx count for K, one for V, per stage)
 //   WG NQT warp 1   MMA issuer (one thread): S_t = Q_t K_j^T  (SS, f16->f32,
 //                   TMEM), then O_t += P_t V_j with P read from TMEM (TS)
 //
@@ -88,7 +88,7 @@ template <int D, int NQT> struct PrefillCfg {
     // while the softmax of the current one is still computing.  Otherwise P
     // aliases S and the next S waits for P V.
     static constexpr bool LA = !ROWSUM && NQT * (128 + 64 + D) <= 512;
-    static constexpr int NBARS = 1 + 2 * STAGES + 4 * NQT + 1;
+    static constexpr int NBARS = 1 + 3 * STAGES + 4 * NQT + 1;
     static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;   // +1024 alignment slack
     static constexpr int NTHREADS = 128 * NQT + 128;
     static constexpr int TMA_WARP = 4 * NQT, MMA_WARP = 4 * NQT + 1;
@@ -191,14 +191,15 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem + C::BAR_OFF);
     uint64_t *q_full = bars;
-    uint64_t *kv_full = bars + 1;                  // K_j and V_j of a stage landed
+    uint64_t *kv_full = bars + 1;                  // K_j of a stage landed (V_j: v_full)
     uint64_t *kv_empty = kv_full + C::STAGES;
     uint64_t *s_full = kv_empty + C::STAGES;
     uint64_t *p_full = s_full + NQT;
     uint64_t *s_free = p_full + NQT;               // LA: S_t copied to registers, may be overwritten
     uint64_t *pv_done = s_free + NQT;              // LA: O_t += P_t V done, P_t may be rewritten
     uint64_t *o_full = pv_done + NQT;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_full + 1);
+    uint64_t *v_full = o_full + 1;                 // V_j of a stage landed
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(v_full + C::STAGES);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // CSL: the instantiation for causal launches with the causal/window flags
@@ -257,6 +258,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
         mbar_init(q_full, a.q_tma ? 1 : 4 * NQT);   // the TMA thread, or one arrival per softmax warp
         for (int s = 0; s < C::STAGES; ++s) {
             mbar_init(&kv_full[s], 1);
+            mbar_init(&v_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
         for (int t = 0; t < NQT; ++t) {
@@ -699,19 +701,21 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     const int y = (j_begin + it) * C::BN;
                     char *ks = smem + C::K_OFF + st * C::TILE_BYTES;
                     char *vs = smem + C::V_OFF + st * C::TILE_BYTES;
-                    mbar_arrive_expect_tx(&kv_full[st], 2 * C::TILE_BYTES);
+                    mbar_arrive_expect_tx(&kv_full[st], C::TILE_BYTES);
+                    mbar_arrive_expect_tx(&v_full[st], C::TILE_BYTES);
 #pragma unroll
                     for (int sub = 0; sub < C::SUB; ++sub)
                         tma_load_4d(ks + sub * 16384, &tmK, &kv_full[st], sub * 64, y, g, bkv);
 #pragma unroll
                     for (int sub = 0; sub < C::SUB; ++sub)
-                        tma_load_4d(vs + sub * 16384, &tmV, &kv_full[st], sub * 64, y, g, bkv);
+                        tma_load_4d(vs + sub * 16384, &tmV, &v_full[st], sub * 64, y, g, bkv);
                 }
                 // Drain: the last STAGES loads must have landed before this CTA's
                 // shared memory is released (already true unless a wait failed).
                 for (int it = issued > C::STAGES ? issued - C::STAGES : 0; it < issued; ++it) {
                     const int st = it % C::STAGES;
                     mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
+                    mbar_wait(&v_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV);
                 }
             }
         } else if (warp == C::MMA_WARP) {
@@ -786,6 +790,10 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                             }
                             if (!good) break;
                         }
+                        if (!__all_sync(0xffffffffu, mbar_wait(&v_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV))) {
+                            good = false;
+                            break;
+                        }
 #pragma unroll
                         for (int t = 0; t < NQT; ++t) {
                             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], it & 1, a.err, VTX_KERR_P))) {
@@ -803,16 +811,23 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 for (int it = 0; !C::LA && it <= n_iter && good; ++it) {
                     const int st = it % C::STAGES;
                     const int pst = (it + C::STAGES - 1) % C::STAGES;
-                    if (it < n_iter &&
-                        !__all_sync(0xffffffffu, mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV)))
-                        break;
-                    tc_fence_after();
+                    // V of the tile whose P V is due (it - 1), K of the one whose
+                    // S is due (it): each waited for just before its first use
+                    bool v_ready = it == 0, k_ready = it == n_iter;
 #pragma unroll
                     for (int t = 0; t < NQT; ++t) {
                         int t_lo, t_hi;
                         tile_iters(t, t_lo, t_hi);
                         const int pi = it - 1;                 // the key tile whose P V is due
                         if (pi >= t_lo && pi < t_hi) {
+                            if (!v_ready) {
+                                if (!__all_sync(0xffffffffu,
+                                                mbar_wait(&v_full[pst], (pi / C::STAGES) & 1, a.err, VTX_KERR_KV))) {
+                                    good = false;
+                                    break;
+                                }
+                                v_ready = true;
+                            }
                             if (!__all_sync(0xffffffffu, mbar_wait(&p_full[t], (pi - t_lo) & 1, a.err, VTX_KERR_P))) {
                                 good = false;
                                 break;
@@ -820,7 +835,18 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                             tc_fence_after();
                             issue_pv(t, pst, pi > t_lo ? 1u : 0u);
                         }
-                        if (it >= t_lo && it < t_hi) issue_qk(t, st);
+                        if (it >= t_lo && it < t_hi) {
+                            if (!k_ready) {
+                                if (!__all_sync(0xffffffffu,
+                                                mbar_wait(&kv_full[st], (it / C::STAGES) & 1, a.err, VTX_KERR_KV))) {
+                                    good = false;
+                                    break;
+                                }
+                                tc_fence_after();
+                                k_ready = true;
+                            }
+                            issue_qk(t, st);
+                        }
                     }
                     if (!good) break;
                     if (it > 0) mma_commit_w(lead, &kv_empty[pst]);
