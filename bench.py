@@ -42,7 +42,7 @@ sys.path.insert(0, os.path.join(ROOT, "voxtral.cpp_b200"))
 ENC = dict(n=1500, H=20, D=64, layers=32)
 DEC = dict(n_seq=256, Hq=32, Hkv=8, D=128, lo=512, hi=16384)
 METRIC_ENC = "attn TFLOP/s (prefill/encoder)"
-ENC_TRAFFIC_BYTES = 11_581_696          # one encoder launch, from the committed ncu capture
+ENC_TRAFFIC_BYTES = 11_590_656          # one encoder launch, dram read + write, from the committed ncu capture
 DEC_TRAFFIC_RATIO_F16 = (1_058_088_000 + 7_246_080) / 1_057_517_568   # (read + write) / KV bytes, 32 streams
 DEC_TRAFFIC_RATIO_Q8 = (562_400_768 + 6_991_872) / 561_806_208     # (read + write) / KV bytes, 32 streams
 METRIC_DEC = "KV GB/s (decode)"
@@ -227,7 +227,7 @@ def run_encoder(args, rank, world, local):
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
                      # dram__bytes_read + dram__bytes_write of one launch, ncu --set full capture
-                     # (profiles/fa_prefill_sm100_encoder_cfg2.md): 11.58 MB read (= Q+K+V), 0 written
+                     # (profiles/fa_prefill_sm100_encoder_cfg2.md): 11.59 MB read (= Q+K+V), 0 written
                      # (the 7.68 MB output stays in L2 during the launch)
                      "traffic": ENC_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
                      "peak_src": f"{peaks['src']} bf16 dense (burst)",
