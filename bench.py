@@ -226,9 +226,9 @@ def run_encoder(args, rank, world, local):
         "audio_sec_per_sec": round(30.0 * args.steps * world / (ms * 1e-3), 1),
         "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peaks["bf16_tflops"],
                      "unit": "TFLOP/s", "frac": round(achieved / peaks["bf16_tflops"], 4),
-                     # dram__bytes_read + dram__bytes_write of one launch, ncu --set full capture
-                     # (profiles/fa_prefill_sm100_encoder_cfg2.md): 11.59 MB read (= Q+K+V), 0 written
-                     # (the 7.68 MB output stays in L2 during the launch)
+                     # dram__bytes_read + dram__bytes_write of one launch in the committed
+                     # ncu --set full capture of the encoder kernel: 11.59 MB read (= Q+K+V),
+                     # 0 written (the 7.68 MB output stays in L2 during the launch)
                      "traffic": ENC_TRAFFIC_BYTES, "traffic_unit": "bytes per launch",
                      "peak_src": f"{peaks['src']} bf16 dense (burst)",
                      "per_launch_ms": round(launch_ms, 5),
@@ -386,8 +386,8 @@ def run_decode(args, rank, world, local):
                    "parallelism": f"dp{world} (independent streams per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / peaks["hbm_gbs"], 4),
-                     # DRAM bytes per KV byte from the committed 32-stream ncu captures
-                     # (profiles/fa_decode_*_cfg5.md): reads = algorithmic KV bytes, + partials
+                     # DRAM bytes per KV byte from the committed 32-stream ncu captures of the
+                     # decode kernels: reads = algorithmic KV bytes, + partials
                      "traffic": round(kv_bytes * (DEC_TRAFFIC_RATIO_Q8 if q8 else DEC_TRAFFIC_RATIO_F16)),
                      "traffic_unit": "bytes per step (scaled from the capture by KV bytes)",
                      "peak_src": f"{peaks['src']} copy bandwidth"},
