@@ -46,15 +46,17 @@ def test_struct_layouts_match_ctypes(tmp_path):
     import vtx_attn
     src = tmp_path / "probe.c"
     src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vtx_fa.h"\n'
-                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(vtx_tensor), sizeof(vtx_fa_params),'
-                   ' sizeof(vtx_decode_batch), offsetof(vtx_tensor, data), offsetof(vtx_decode_batch, q),'
-                   ' sizeof(vtx_block_q8_0)); return 0;}\n')
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu %zu %zu\\n", sizeof(vtx_tensor),'
+                   ' sizeof(vtx_fa_params), sizeof(vtx_decode_batch), offsetof(vtx_tensor, data),'
+                   ' offsetof(vtx_decode_batch, q), sizeof(vtx_block_q8_0), offsetof(vtx_decode_batch, scale),'
+                   ' offsetof(vtx_decode_batch, fresh_row)); return 0;}\n')
     exe = tmp_path / "probe"
     subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
     vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
     assert vals == [ctypes.sizeof(vtx_attn.VtxTensor), ctypes.sizeof(vtx_attn.FaParams),
                     ctypes.sizeof(vtx_attn.DecodeBatch), vtx_attn.VtxTensor.data.offset,
-                    vtx_attn.DecodeBatch.q.offset, 34]
+                    vtx_attn.DecodeBatch.q.offset, 34, vtx_attn.DecodeBatch.scale.offset,
+                    vtx_attn.DecodeBatch.fresh_row.offset]
 
 
 def test_kv_append_args_layout(tmp_path):
