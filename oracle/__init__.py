@@ -66,6 +66,19 @@ def build(force: bool = False) -> str:
     return _LIB_PATH
 
 
+def build_ref() -> str | None:
+    """Compile oracle/_ref/enc_tokens_ref from the reference's own sources
+    (`src/voxtral.cpp` encoder token-count functions, extracted by the
+    Makefile's `ref` target) when the reference tree sits beside this
+    repository; None when it does not.  The binary only generates
+    tests/golden/enc_chunks.json; nothing at run time needs it."""
+    ref_src = os.path.join(_HERE, "..", "..", "reference", "src", "voxtral.cpp")
+    if not os.path.exists(ref_src):
+        return None
+    subprocess.run(["make", "-s", "-C", _HERE, "ref"], check=True)
+    return os.path.join(_HERE, "_ref", "enc_tokens_ref")
+
+
 def lib():
     global _lib
     if _lib is None:
