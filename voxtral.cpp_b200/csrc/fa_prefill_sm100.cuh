@@ -508,8 +508,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             }
             const float neg_m = m_run == -INFINITY ? 0.0f : -m_run;
             // P = 2^(x*cx - m): MUFU for most pairs, FMA-pipe polynomial for the rest
+            // With the tensor-core row sum each pair is packed to halves as soon
+            // as it is computed; otherwise the f32 values are summed first.
             uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
             const uint64_t cx2 = pk2(cx, cx), nm2 = pk2(neg_m, neg_m);
+            uint32_t pk[64];
 #pragma unroll
             for (int pi = 0; pi < 64; ++pi) {
                 float e0, e1;
@@ -520,9 +523,13 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     e0 = ex2(e0);
                     e1 = ex2(e1);
                 }
-                s[2 * pi] = e0;
-                s[2 * pi + 1] = e1;
-                if (!C::ROWSUM) sum2[pi & 3] = fadd2(sum2[pi & 3], pk2(e0, e1));
+                if (C::ROWSUM) {
+                    pk[pi] = pack_half2(e0, e1);
+                } else {
+                    s[2 * pi] = e0;
+                    s[2 * pi + 1] = e1;
+                    sum2[pi & 3] = fadd2(sum2[pi & 3], pk2(e0, e1));
+                }
             }
             if (!C::ROWSUM) {
                 const uint64_t s01 = fadd2(fadd2(sum2[0], sum2[1]), fadd2(sum2[2], sum2[3]));
@@ -532,9 +539,10 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             }
             // P packed to half pairs before any wait, so the conversions can be
             // scheduled among the exponentials
-            uint32_t pk[64];
+            if (!C::ROWSUM) {
 #pragma unroll
-            for (int i = 0; i < 64; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+                for (int i = 0; i < 64; ++i) pk[i] = pack_half2(s[2 * i], s[2 * i + 1]);
+            }
             if (C::LA && it > t_lo) {               // P_t and O_t are free once the previous P V retired
                 ok = __all_sync(0xffffffffu, mbar_wait(&pv_done[t], (it - t_lo - 1) & 1, a.err, VTX_KERR_O));
                 if (!ok) break;
