@@ -206,6 +206,7 @@ def run_encoder(args, rank, world, local):
     value = flop_step * args.steps * world / (ms * 1e-3) / 1e12
     launch_ms = ms_local / (args.steps * L)
     err = vtx_attn.read_device_error(stream)
+    parity = check_encoder_layer(qkv[0], out[0]) if (rank == 0 and not args.no_check) else None
 
     # ---- end to end through the public call, host buffers ----------------------
     e2e = run_encoder_e2e(args, dev, world, rank)
@@ -237,6 +238,7 @@ def run_encoder(args, rank, world, local):
         "gpu_launches": args.steps * L,
         "clocks": clocks.summary(),
         "device_error": err,
+        "parity": parity,
     }
     return res
 
@@ -322,6 +324,66 @@ def cpu_baseline_encoder(budget_s: float = 12.0):
 
 
 # ---- decode workload ---------------------------------------------------------------
+def make_decode_inputs(S: int, q8: bool, seed_np: int, seed_dev: int, dev):
+    """configs[4] inputs: S streams with kv_len ~ U[512, 16384] (numpy seed),
+    per stream a K and a V cache of kv_len rows x 8 KV heads x 128 drawn
+    N(0,1) on the device (torch seed), stored f16 or quantized to Q8_0 by
+    ggml's rule; Q (S, 32, 128) F32 N(0,1)."""
+    import numpy as np
+    import torch
+    import vtx_attn
+    Hq, Hkv, D = DEC["Hq"], DEC["Hkv"], DEC["D"]
+    rng = np.random.default_rng(seed_np)
+    lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
+    g = torch.Generator(device=dev)
+    g.manual_seed(seed_dev)
+
+    def cache(L):
+        x = torch.randn((int(L), Hkv, D), generator=g, device=dev)
+        return vtx_attn.quantize_q8_0(x) if q8 else x.to(torch.float16)
+
+    ks = [cache(L) for L in lens]
+    vs = [cache(L) for L in lens]
+    q = torch.randn((S, Hq, D), generator=g, device=dev)
+    return lens, ks, vs, q
+
+
+def check_decode_rows(q, ks, vs, lens, out, q8: bool, n_check: int = 8, seed: int = 0):
+    """Checker (outside every timed region): the oracle's ggml-mode batched
+    decode on a seeded sample of n_check streams against the device output
+    rows of the same streams, judged by oracle.parity_verdict (fp64 truth
+    and ggml mode, ggml's own half-precision drift admitted)."""
+    import numpy as np
+    import oracle as O
+    Hkv, D = DEC["Hkv"], DEC["D"]
+    row = D // 32 * 34 if q8 else D * 2
+    idx = sorted(np.random.default_rng(seed).choice(len(lens), size=min(n_check, len(lens)), replace=False).tolist())
+    kl = [ks[i].cpu().numpy() for i in idx]
+    vl = [vs[i].cpu().numpy() for i in idx]
+    args = (q[idx].cpu().numpy(), kl, vl, lens[idx], 1.0 / D ** 0.5, O.Q8_0 if q8 else O.F16, Hkv, Hkv * row, row)
+    ref = O.decode_batched(*args)
+    truth = O.decode_batched(*args, mode=O.MODE_FP64)
+    v = O.parity_verdict(out[idx].cpu().numpy(), ref, truth)
+    v["sample"] = f"streams {idx} of {len(lens)} (every head), oracle ggml mode and fp64"
+    return v
+
+
+def check_encoder_layer(qkv_l, out_l):
+    """Checker (outside every timed region): one timed encoder layer's output
+    against the oracle's flash_attn_ext (ggml mode and fp64) on the same f16
+    Q/K/V, judged by oracle.parity_verdict."""
+    import numpy as np
+    import oracle as O
+    D = ENC["D"]
+    q, k, v = (qkv_l[i].cpu().numpy() for i in range(3))            # (n, H, D) f16 each
+    view = lambda a: a.transpose(1, 0, 2)[None]
+    ref = O.flash_attn_ext(view(q), view(k), view(v), None, D ** -0.5)
+    truth = O.flash_attn_ext(view(q), view(k), view(v), None, D ** -0.5, mode=O.MODE_FP64)
+    v = O.parity_verdict(out_l.cpu().numpy(), ref, truth)
+    v["sample"] = "layer 0 of the timed graph, all 20 heads x 1500 tokens, oracle ggml mode and fp64"
+    return v
+
+
 def run_decode(args, rank, world, local):
     import numpy as np
     import torch
@@ -329,30 +391,12 @@ def run_decode(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     S, Hq, Hkv, D = args.streams, DEC["Hq"], DEC["Hkv"], DEC["D"]
-    rng = np.random.default_rng(4321 + rank)
-    lens = rng.integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
-    g = torch.Generator(device=dev)
-    g.manual_seed(77 + rank)
     q8 = getattr(args, "kv", "f16") == "q8_0"
     row = D // 32 * 34 if q8 else D * 2                   # bytes of one head's K (or V) row
-
-    def cache(L):
-        if not q8:
-            return torch.randn((int(L), Hkv, D), generator=g, device=dev).to(torch.float16)
-        # ggml Q8_0 blocks {f16 d; int8 qs[32]}: qs ~ U[-127, 127], d ~ U[0.005, 0.05]
-        blk = torch.empty((int(L), Hkv, D // 32, 34), dtype=torch.uint8, device=dev)
-        blk[..., 2:] = torch.randint(-127, 128, blk[..., 2:].shape, generator=g, device=dev,
-                                     dtype=torch.int16).to(torch.int8).view(torch.uint8)
-        d = (torch.rand(blk.shape[:-1], generator=g, device=dev) * 0.045 + 0.005).to(torch.float16)
-        blk[..., :2] = d.unsqueeze(-1).view(torch.uint8).reshape(*blk.shape[:-1], 2)
-        return blk
-
-    ks = [cache(L) for L in lens]
-    vs = [cache(L) for L in lens]
+    lens, ks, vs, q = make_decode_inputs(S, q8, 4321 + rank, 77 + rank, dev)
     plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D,
                                     vtx_attn.Q8_0 if q8 else vtx_attn.F16, Hkv * row, row, int(lens.max()),
                                     1.0 / D ** 0.5)
-    q = torch.randn((S, Hq, D), generator=g, device=dev)
     out = torch.empty_like(q)
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -374,11 +418,15 @@ def run_decode(args, rank, world, local):
     value = kv_bytes * args.steps * world / (ms * 1e-3) / 1e9
     peaks = load_peaks()
     achieved = kv_bytes / (ms_local / args.steps * 1e-3) / 1e9
+    parity = check_decode_rows(q, ks, vs, lens, out, q8) if (rank == 0 and not getattr(args, "no_check", False)) \
+        else None
     return {
+        "parity": parity,
         "metric": METRIC_DEC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "q8_0" if q8 else "f16",
-        "data": ("synthetic Q8_0 KV (int8 U[-127,127], f16 scales)" if q8 else "synthetic N(0,1) f16 KV")
+        "data": ("synthetic N(0,1) KV quantized to Q8_0 by ggml's rule (quantize_row_q8_0_ref)" if q8
+                 else "synthetic N(0,1) f16 KV")
                 + ", ragged lengths U[512,16384] seeded per rank",
         "config": {"workload": f"configs[4] batched decode: {S} streams, GQA 32/8 x 128, "
                                f"{'Q8_0' if q8 else 'f16'} KV, 1 layer per step",
@@ -785,6 +833,7 @@ def main():
     ap.add_argument("--workload", default="encoder",
                     choices=["encoder", "decode", "kv_append", "decode_step", "realtime", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true", help="skip the oracle check of the timed outputs")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="decode workload: KV cache type")
@@ -812,7 +861,8 @@ def main():
             for kv, key in (("f16", "decode"), ("q8_0", "decode_q8_0")):
                 dargs.kv = kv
                 d = run_decode(dargs, rank, world, local)
-                res[key] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "roofline", "config")}
+                res[key] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "roofline", "config",
+                                              "data", "parity")}
                 torch.cuda.empty_cache()
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()

@@ -357,3 +357,31 @@ def encoder_stitch(chunk_out: np.ndarray, chunks, n_rows: int) -> np.ndarray:
     for c, ch in enumerate(chunks):
         out[ch["write_offset"]:ch["write_offset"] + ch["stride"]] = chunk_out[c, ch["skip"]:ch["skip"] + ch["stride"]]
     return out
+
+
+# ---- the parity criterion ------------------------------------------------------
+ATOL, RTOL = 2e-3, 1e-2          # BASELINE north_star tolerance (fp32 accumulate on the GPU)
+
+
+def parity_verdict(got: np.ndarray, ggml: np.ndarray, fp64: np.ndarray) -> dict:
+    """Judges a device result against the oracle run in both modes.
+
+    * vs fp64 truth: |got - fp64| <= ATOL + RTOL |fp64| everywhere.
+    * vs ggml mode:  |got - ggml| <= ATOL + RTOL |ggml| + |ggml - fp64|.
+      ggml's CPU kernel accumulates P.V in half precision when V is F16
+      (VKQ16), so over thousands of keys its own result drifts from exact
+      arithmetic by up to a few 1e-3 -- above ATOL.  A device that
+      accumulates in fp32 then differs from ggml by ggml's own rounding; the
+      bound admits exactly that per-element drift and nothing more.  For
+      F32 / Q8_0 V (f32 accumulator in ggml) the drift term is ~1e-6.
+    Returns the maxima and the verdict."""
+    got = got.astype(np.float64)
+    g = ggml.astype(np.float64)
+    f = fp64.astype(np.float64)
+    e_g, e_f, drift = np.abs(got - g), np.abs(got - f), np.abs(g - f)
+    ok_f = bool(np.all(e_f <= ATOL + RTOL * np.abs(f)))
+    ok_g = bool(np.all(e_g <= ATOL + RTOL * np.abs(g) + drift))
+    return {"max_abs_err_vs_ggml": float(e_g.max()) if e_g.size else 0.0,
+            "max_abs_err_vs_fp64": float(e_f.max()) if e_f.size else 0.0,
+            "ggml_max_drift_from_fp64": float(drift.max()) if drift.size else 0.0,
+            "ok_vs_fp64": ok_f, "ok_vs_ggml": ok_g, "ok": ok_f and ok_g}

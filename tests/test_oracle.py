@@ -122,3 +122,31 @@ def test_decode_batched_matches_single_calls():
         one = O.flash_attn_ext(q[s][None, :, None, :], ks[s].transpose(1, 0, 2)[None],
                                vs[s].transpose(1, 0, 2)[None], None, 0.125)
         assert np.array_equal(out[s], one[0, 0])
+
+
+def test_torch_q8_0_quantizer_matches_ggml_rule_on_cpu():
+    """vtx_attn.quantize_q8_0 (the bench's Q8_0 data path) equals the oracle's
+    quantize_row_q8_0_ref byte for byte, zero blocks and ties included."""
+    import torch
+    import vtx_attn
+    x = np.random.default_rng(11).standard_normal((64, 8, 128)).astype(np.float32)
+    x[1, 2, :32] = 0.0
+    x[2, 0, :32] = np.arange(32, dtype=np.float32) - 15.5          # exact halves after scaling
+    got = vtx_attn.quantize_q8_0(torch.from_numpy(x)).numpy()
+    assert np.array_equal(got, O.quantize_q8_0(x))
+
+
+def test_parity_verdict_admits_ggml_drift_only():
+    """The criterion used at the benchmark's sizes: a result at fp64 truth
+    passes even where ggml mode itself drifts past ATOL, while an error
+    planted in the oracle's ggml output (ggml drifting where the candidate
+    does not follow) or a candidate off truth by more than ATOL fails."""
+    f = np.linspace(-0.3, 0.3, 1000)
+    g = f.copy()
+    g[10] += 3e-3                                   # ggml's own half-precision drift
+    assert O.parity_verdict(f.copy(), g, f)["ok"]
+    assert O.parity_verdict(g.copy(), g, f)["ok_vs_ggml"]
+    bad = f.copy()
+    bad[500] += 3e-3                                # candidate off truth (|f| ~ 0) where ggml is exact
+    v = O.parity_verdict(bad, g, f)
+    assert not v["ok_vs_fp64"] and not v["ok_vs_ggml"] and not v["ok"]

@@ -104,3 +104,12 @@ def _failing_worker(rank, world, port):
         shard.head_split_prefill(q, k, k, None, 0.125, attn=_oracle_attn)
     finally:
         dist.destroy_process_group()
+
+
+def test_head_split_prefill_rejects_alibi():
+    """ggml's ALiBi slopes depend on the global head index, which a rank's
+    call on its head slice does not see: the split refuses max_bias != 0."""
+    q = torch.zeros((1, 8, 4, 64))
+    k = torch.zeros((1, 4, 4, 64))
+    with pytest.raises(ValueError):
+        shard.head_split_prefill(q, k, k, None, 0.125, attn=_oracle_attn, max_bias=8.0)

@@ -110,3 +110,13 @@ def assert_close(got: np.ndarray, ref: np.ndarray, what: str, atol=ATOL, rtol=RT
         idx = np.unravel_index(np.argmax(err - bound), err.shape)
         raise AssertionError(f"{what}: {bad.sum()} / {err.size} elements outside atol={atol} rtol={rtol}; "
                              f"worst at {idx}: got {got[idx]} ref {ref[idx]} (max abs err {err.max():.3e})")
+
+
+def assert_parity(got: np.ndarray, ggml: np.ndarray, fp64: np.ndarray, what: str) -> dict:
+    """oracle.parity_verdict as an assertion (the bound for sizes where ggml's
+    half-precision V accumulator drifts from exact arithmetic by more than
+    ATOL): within tolerance of fp64 truth everywhere, and of ggml up to
+    ggml's own per-element drift."""
+    v = O.parity_verdict(got, ggml, fp64)
+    assert v["ok"], f"{what}: {v}"
+    return v

@@ -18,6 +18,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <utility>
 
@@ -41,41 +42,42 @@ namespace {
 constexpr int kMaxDevices = 64;
 
 struct DeviceState {
-    int ready = 0;
     int ok = 0;
     int sms = 148;
     int *err = nullptr;
 };
 DeviceState g_dev[kMaxDevices];
-std::mutex g_mu;
+std::once_flag g_dev_once[kMaxDevices];
+std::once_flag g_encode_once;
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
+// Per-device set-up runs exactly once (std::call_once), so concurrent first
+// calls from several host threads are ordered: every caller sees the state
+// the one initialising call wrote.
 int ensure_device(DeviceState **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VTX_ERR_NO_DEVICE;
     DeviceState &s = g_dev[dev];
-    if (!s.ready) {
-        std::lock_guard<std::mutex> lk(g_mu);
-        if (!s.ready) {
-            int major = 0, minor = 0;
-            cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
-            cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
-            cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev);
-            s.ok = (major == 10 && minor == 0);
-            void *p = nullptr;
-            if (s.ok && cudaGetSymbolAddress(&p, g_vtx_kernel_err) != cudaSuccess) s.ok = 0;
-            s.err = static_cast<int *>(p);
-            if (s.ok && !g_encode) {
+    std::call_once(g_dev_once[dev], [&] {
+        int major = 0, minor = 0;
+        cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+        cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+        cudaDeviceGetAttribute(&s.sms, cudaDevAttrMultiProcessorCount, dev);
+        s.ok = (major == 10 && minor == 0);
+        void *p = nullptr;
+        if (s.ok && cudaGetSymbolAddress(&p, g_vtx_kernel_err) != cudaSuccess) s.ok = 0;
+        s.err = static_cast<int *>(p);
+        if (s.ok) {
+            std::call_once(g_encode_once, [] {
                 cudaDriverEntryPointQueryResult q;
                 void *fn = nullptr;
                 if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) == cudaSuccess &&
                     q == cudaDriverEntryPointSuccess)
                     g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
-            }
-            cudaGetLastError();
-            s.ready = 1;
+            });
         }
-    }
+        cudaGetLastError();
+    });
     if (!s.ok) return VTX_ERR_NO_DEVICE;
     *out = &s;
     return VTX_OK;
@@ -418,14 +420,14 @@ int launch_combine(const SplitArgs &a, int gy, cudaStream_t st) {
 template <int D, int KVT, int MAXR>
 int launch_split_t(const SplitArgs &a, dim3 grid, cudaStream_t st) {
     constexpr int smem = splitkv_smem_bytes<D, KVT, MAXR>();
-    static int attr_done[kMaxDevices] = {0};
+    static std::atomic<int> attr_done[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_done[dev]) {
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(fa_splitkv_kernel<D, KVT, MAXR>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
             cudaSuccess)
             return VTX_ERR_CUDA;
-        attr_done[dev] = 1;
+        attr_done[dev].store(1, std::memory_order_release);
     }
     if (launch_pdl(fa_splitkv_kernel<D, KVT, MAXR>, grid, dim3(128), smem, st, a) != VTX_OK) return VTX_ERR_CUDA;
     if (!a.write_final) {
@@ -444,14 +446,14 @@ int launch_split_d(const SplitArgs &a, int maxr, dim3 grid, cudaStream_t st) {
 template <int D>
 int launch_decode_mma_t(const SplitArgs &a, cudaStream_t st) {
     using C = DecodeCfg<D>;
-    static int attr_done[kMaxDevices] = {0};
+    static std::atomic<int> attr_done[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_done[dev]) {
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(fa_decode_mma_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
             cudaSuccess)
             return VTX_ERR_CUDA;
-        attr_done[dev] = 1;
+        attr_done[dev].store(1, std::memory_order_release);
     }
     const long long items = (long long)a.B * a.Hkv * a.n_splits;
     if (launch_pdl(fa_decode_mma_kernel<D>, dim3((unsigned)((items + C::WARPS - 1) / C::WARPS)), dim3(128), C::SMEM,
@@ -483,14 +485,14 @@ int decode_q8_hpc(int kv_type, int D, int n_q, int G, int Hkv, int maxr, int n_h
 
 int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
     using C = DecodeQ8Cfg<128>;
-    static int attr_done[kMaxDevices] = {0};
+    static std::atomic<int> attr_done[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_done[dev]) {
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(fa_decode_q8_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
             cudaSuccess)
             return VTX_ERR_CUDA;
-        attr_done[dev] = 1;
+        attr_done[dev].store(1, std::memory_order_release);
     }
     const long long items = (long long)a.B * (a.Hkv / hpc) * a.n_splits;
     if (items > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
@@ -555,14 +557,14 @@ template <int D, int NQT, bool HM, bool UF, bool CSL = false>
 int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const CUtensorMap &mq,
                      const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     using C = PrefillCfg<D, NQT>;
-    static int attr_done[kMaxDevices] = {0};
+    static std::atomic<int> attr_done[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
-    if (!attr_done[dev]) {
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
         if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return VTX_ERR_CUDA;
-        attr_done[dev] = 1;
+        attr_done[dev].store(1, std::memory_order_release);
     }
     return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo,
                       mq, a);
@@ -595,6 +597,72 @@ size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, con
     const PrefillPlan pp = plan_prefill(g, q, k, v, sms, false);   // the tile split does not change the workspace
     if (pp.use) return pp.conv_bytes;
     return plan_split(g, sms, g.n_kv, false).part_bytes;
+}
+
+
+// The batched ragged decode shared by vtx_flash_attn_decode_batched (scratch =
+// the caller's workspace) and vtx_flash_attn_decode_batched_noalloc (scratch =
+// the library's built-in buffer, looked up through get_scratch once the batch
+// is known to fit).  too_big is the status returned when the split partials do
+// not fit in scratch_bytes.
+int decode_batched_impl(const vtx_decode_batch *b, void *scratch, size_t scratch_bytes, cudaStream_t st, int too_big,
+                        int (*get_scratch)(void **)) {
+    if (!b) return VTX_ERR_NULL;
+    if (b->n_seq < 0 || b->n_head_q <= 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv || b->max_kv_len < 0)
+        return VTX_ERR_SHAPE;
+    if (b->head_dim != 64 && b->head_dim != 128) return VTX_ERR_UNSUPPORTED;
+    if (b->kv_type != VTX_TYPE_F16 && b->kv_type != VTX_TYPE_F32 && b->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    if (b->n_seq == 0) return VTX_OK;
+    if (!b->q || !b->k_ptrs || !b->v_ptrs || !b->kv_len || !b->dst) return VTX_ERR_NULL;
+    if (b->n_seq > 65535 || b->n_head_q / b->n_head_kv > 16) return VTX_ERR_UNSUPPORTED;
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    const int D = b->head_dim;
+    Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
+          b->n_seq, b->kv_type};
+    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b));
+    if (scratch_bytes < sp.part_bytes) return too_big;
+    if (get_scratch && sp.part_bytes) {
+        rc = get_scratch(&scratch);
+        if (rc != VTX_OK) return rc;
+    }
+    if (scratch && reinterpret_cast<uintptr_t>(scratch) % 256) return VTX_ERR_WORKSPACE;
+    SplitArgs a{};
+    a.q = reinterpret_cast<const char *>(b->q);
+    a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
+    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len; a.fresh = b->fresh_row;
+    a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
+    a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
+    a.k_bdiv = a.v_bdiv = 1;
+    a.n_kv = g.n_kv;
+    a.dst = reinterpret_cast<char *>(b->dst);
+    a.d_nb1 = (long long)D * 4; a.d_nb2 = (long long)b->n_head_q * D * 4; a.d_nb3 = (long long)b->n_head_q * D * 4;
+    a.n_q = 1; a.Hq = b->n_head_q; a.Hkv = b->n_head_kv; a.G = g.G; a.B = b->n_seq;
+    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
+    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
+    float qk_scale, softcap, m0, m1;
+    int nhl2;
+    fill_math(b->scale, 0.0f, 0.0f, b->n_head_q, &qk_scale, &softcap, &m0, &m1, &nhl2);
+    a.qk_scale = qk_scale; a.softcap = 0.0f; a.max_bias = 0.0f; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
+    a.write_final = sp.n_splits <= 1;
+    if (!a.write_final) {
+        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
+        a.part_o = static_cast<float *>(scratch);
+        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(scratch) + align_up(work * D * 4, 256));
+    }
+    const int rb = row_bytes(b->kv_type, D);
+    a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
+    // stream base pointers are only known on the device: require 16-byte
+    // aligned bases whenever the strides allow 16-byte copies
+    if (!a.vec) return VTX_ERR_STRIDE;
+    a.err = ds->err;
+    if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks)) return launch_decode_mma(a, D, st);
+    if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
+                                      a.v_nb1, a.v_nb2))
+        return launch_decode_q8(a, hpc, st);
+    dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
+    return launch_split(a, D, b->kv_type, sp.maxr, grid, st);
 }
 
 }  // namespace
@@ -784,59 +852,8 @@ size_t vtx_flash_attn_decode_batched_workspace(const vtx_decode_batch *b) {
 }
 
 int vtx_flash_attn_decode_batched(const vtx_decode_batch *b, void *workspace, size_t workspace_bytes, void *stream) {
-    if (!b) return VTX_ERR_NULL;
-    if (b->n_seq < 0 || b->n_head_q <= 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv || b->max_kv_len < 0)
-        return VTX_ERR_SHAPE;
-    if (b->head_dim != 64 && b->head_dim != 128) return VTX_ERR_UNSUPPORTED;
-    if (b->kv_type != VTX_TYPE_F16 && b->kv_type != VTX_TYPE_F32 && b->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
-    if (b->n_seq == 0) return VTX_OK;
-    if (!b->q || !b->k_ptrs || !b->v_ptrs || !b->kv_len || !b->dst) return VTX_ERR_NULL;
-    if (b->n_seq > 65535 || b->n_head_q / b->n_head_kv > 16) return VTX_ERR_UNSUPPORTED;
-    DeviceState *ds = nullptr;
-    int rc = ensure_device(&ds);
-    if (rc != VTX_OK) return rc;
-    const int D = b->head_dim;
-    Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
-          b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b));
-    if (workspace_bytes < sp.part_bytes) return VTX_ERR_WORKSPACE;
-    if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
-    SplitArgs a{};
-    a.q = reinterpret_cast<const char *>(b->q);
-    a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
-    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len; a.fresh = b->fresh_row;
-    a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
-    a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
-    a.k_bdiv = a.v_bdiv = 1;
-    a.n_kv = g.n_kv;
-    a.dst = reinterpret_cast<char *>(b->dst);
-    a.d_nb1 = (long long)D * 4; a.d_nb2 = (long long)b->n_head_q * D * 4; a.d_nb3 = (long long)b->n_head_q * D * 4;
-    a.n_q = 1; a.Hq = b->n_head_q; a.Hkv = b->n_head_kv; a.G = g.G; a.B = b->n_seq;
-    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
-    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
-    float qk_scale, softcap, m0, m1;
-    int nhl2;
-    fill_math(b->scale, 0.0f, 0.0f, b->n_head_q, &qk_scale, &softcap, &m0, &m1, &nhl2);
-    a.qk_scale = qk_scale; a.softcap = 0.0f; a.max_bias = 0.0f; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
-    a.write_final = sp.n_splits <= 1;
-    if (!a.write_final) {
-        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
-        a.part_o = static_cast<float *>(workspace);
-        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(workspace) + align_up(work * D * 4, 256));
-    }
-    const int rb = row_bytes(b->kv_type, D);
-    a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
-    // stream base pointers are only known on the device: require 16-byte
-    // aligned bases whenever the strides allow 16-byte copies
-    if (!a.vec) return VTX_ERR_STRIDE;
-    a.err = ds->err;
-    if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
-        return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
-    if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
-                                      a.v_nb1, a.v_nb2))
-        return launch_decode_q8(a, hpc, static_cast<cudaStream_t>(stream));
-    dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
-    return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
+    return decode_batched_impl(b, workspace, workspace_bytes, static_cast<cudaStream_t>(stream), VTX_ERR_WORKSPACE,
+                               nullptr);
 }
 
 int vtx_kv_append(const vtx_kv_append_args *p, void *stream) {
@@ -1004,80 +1021,33 @@ int vtx_read_device_error(void *stream) {
 static __device__ __align__(256) unsigned char g_vtx_noalloc_scratch[VTX_NOALLOC_SCRATCH_BYTES];
 
 namespace {
-void *g_noalloc_ptr[kMaxDevices] = {nullptr};
+std::atomic<void *> g_noalloc_ptr[kMaxDevices];
 std::mutex g_noalloc_mu;
 
+// Device address of g_vtx_noalloc_scratch on the current device, looked up
+// once per device while that device is current (acquire/release, so a second
+// host thread sees either null or the complete address).
 int noalloc_scratch(void **out) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return VTX_ERR_NO_DEVICE;
-    if (!g_noalloc_ptr[dev]) {
+    void *p = g_noalloc_ptr[dev].load(std::memory_order_acquire);
+    if (!p) {
         std::lock_guard<std::mutex> lk(g_noalloc_mu);
-        if (!g_noalloc_ptr[dev]) {
-            void *p = nullptr;
+        p = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+        if (!p) {
             if (cudaGetSymbolAddress(&p, g_vtx_noalloc_scratch) != cudaSuccess || !p) {
                 cudaGetLastError();
                 return VTX_ERR_CUDA;
             }
-            g_noalloc_ptr[dev] = p;
+            g_noalloc_ptr[dev].store(p, std::memory_order_release);
         }
     }
-    *out = g_noalloc_ptr[dev];
+    *out = p;
     return VTX_OK;
 }
 }  // namespace
 
 extern "C" int vtx_flash_attn_decode_batched_noalloc(const vtx_decode_batch *b, void *stream) {
-    if (!b) return VTX_ERR_NULL;
-    if (b->n_seq < 0 || b->n_head_q <= 0 || b->n_head_kv <= 0 || b->n_head_q % b->n_head_kv || b->max_kv_len < 0)
-        return VTX_ERR_SHAPE;
-    if (b->head_dim != 64 && b->head_dim != 128) return VTX_ERR_UNSUPPORTED;
-    if (b->kv_type != VTX_TYPE_F16 && b->kv_type != VTX_TYPE_F32 && b->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
-    if (b->n_seq == 0) return VTX_OK;
-    if (!b->q || !b->k_ptrs || !b->v_ptrs || !b->kv_len || !b->dst) return VTX_ERR_NULL;
-    if (b->n_seq > 65535 || b->n_head_q / b->n_head_kv > 16) return VTX_ERR_UNSUPPORTED;
-    DeviceState *ds = nullptr;
-    int rc = ensure_device(&ds);
-    if (rc != VTX_OK) return rc;
-    const int D = b->head_dim;
-    Geo g{D, 1, std::max(1, b->max_kv_len), b->n_head_q, b->n_head_kv, b->n_head_q / b->n_head_kv, b->n_seq,
-          b->n_seq, b->kv_type};
-    const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, true, batch_streaming(b), batch_q8_ctas(b));
-    if (sp.part_bytes > (size_t)VTX_NOALLOC_SCRATCH_BYTES) return VTX_ERR_SCRATCH_LIMIT;
-    void *scratch = nullptr;
-    rc = noalloc_scratch(&scratch);
-    if (rc != VTX_OK) return rc;
-    SplitArgs a{};
-    a.q = reinterpret_cast<const char *>(b->q);
-    a.q_nb1 = (long long)b->n_head_q * D * 4; a.q_nb2 = (long long)D * 4; a.q_nb3 = (long long)b->n_head_q * D * 4;
-    a.k_ptrs = b->k_ptrs; a.v_ptrs = b->v_ptrs; a.kv_len = b->kv_len; a.fresh = b->fresh_row;
-    a.k_nb1 = a.v_nb1 = (long long)b->kv_nb1;
-    a.k_nb2 = a.v_nb2 = (long long)b->kv_nb2;
-    a.k_bdiv = a.v_bdiv = 1;
-    a.n_kv = g.n_kv;
-    a.dst = reinterpret_cast<char *>(b->dst);
-    a.d_nb1 = (long long)D * 4; a.d_nb2 = (long long)b->n_head_q * D * 4; a.d_nb3 = (long long)b->n_head_q * D * 4;
-    a.n_q = 1; a.Hq = b->n_head_q; a.Hkv = b->n_head_kv; a.G = g.G; a.B = b->n_seq;
-    a.tok_per_cta = sp.tok_per_cta; a.hc = sp.hc; a.n_hchunks = sp.n_hchunks; a.n_qtiles = sp.n_qtiles;
-    a.chunk = sp.chunk; a.n_splits = sp.n_splits;
-    float qk_scale, softcap, m0, m1;
-    int nhl2;
-    fill_math(b->scale, 0.0f, 0.0f, b->n_head_q, &qk_scale, &softcap, &m0, &m1, &nhl2);
-    a.qk_scale = qk_scale; a.softcap = 0.0f; a.max_bias = 0.0f; a.m0 = m0; a.m1 = m1; a.n_head_log2 = nhl2;
-    a.write_final = sp.n_splits <= 1;
-    if (!a.write_final) {
-        const size_t work = (size_t)g.B * g.Hkv * sp.n_hchunks * sp.n_qtiles * sp.n_splits * sp.maxr;
-        a.part_o = static_cast<float *>(scratch);
-        a.part_ml = reinterpret_cast<float *>(static_cast<char *>(scratch) + align_up(work * D * 4, 256));
-    }
-    const int rb = row_bytes(b->kv_type, D);
-    a.vec = pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
-    if (!a.vec) return VTX_ERR_STRIDE;
-    a.err = ds->err;
-    if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks))
-        return launch_decode_mma(a, D, static_cast<cudaStream_t>(stream));
-    if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
-                                      a.v_nb1, a.v_nb2))
-        return launch_decode_q8(a, hpc, static_cast<cudaStream_t>(stream));
-    dim3 grid((unsigned)sp.n_splits, (unsigned)(g.Hkv * sp.n_hchunks), (unsigned)b->n_seq);
-    return launch_split(a, D, b->kv_type, sp.maxr, grid, static_cast<cudaStream_t>(stream));
+    return decode_batched_impl(b, nullptr, (size_t)VTX_NOALLOC_SCRATCH_BYTES, static_cast<cudaStream_t>(stream),
+                               VTX_ERR_SCRATCH_LIMIT, noalloc_scratch);
 }

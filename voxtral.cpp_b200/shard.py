@@ -60,6 +60,10 @@ def head_split_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: 
     result on every rank (ggml's permuted dst), assembled with one
     all_gather_into_tensor of the per-rank (B, n_q, Hq/N, Dv) slices."""
     import torch.distributed as dist
+    if float(kw.get("max_bias", 0.0)) != 0.0:
+        # ggml's ALiBi slope depends on the global head index; each rank's
+        # call numbers its heads from 0, so slopes would be wrong past rank 0
+        raise ValueError("head_split_prefill does not support max_bias != 0 (ALiBi)")
     if attn is None:
         import vtx_attn
         attn = vtx_attn.flash_attn_ext

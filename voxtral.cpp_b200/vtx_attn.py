@@ -359,3 +359,24 @@ def window_mask(n: int, window: int = 750, device=None) -> torch.Tensor:
     kj = torch.arange(n, device=device)[None, :]
     allow = (kj <= qi) & (kj >= (qi - (window - 1)).clamp(min=0))
     return torch.where(allow, 0.0, float("-inf")).to(torch.float16)
+
+
+def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
+    """ggml's reference Q8_0 quantizer (quantize_row_q8_0_ref, the rule the
+    reference's converter uses for Q8_0 tensors) over the last axis of a float
+    tensor, on x's device: per 32 values d = amax/127 (stored as f16),
+    q = round-half-away(x / d).  Returns uint8 with the last axis holding
+    D/32 blocks of 34 bytes {f16 d; int8 qs[32]}.  A data-preparation helper
+    for caches built outside vtx_kv_append (which quantizes on write)."""
+    D = x.shape[-1]
+    if D % QK8_0:
+        raise VtxError(-3, "last axis must be a multiple of 32")
+    xb = x.float().reshape(*x.shape[:-1], D // QK8_0, QK8_0)
+    d = xb.abs().amax(dim=-1) / 127.0
+    inv = torch.where(d != 0, 1.0 / d, torch.zeros_like(d))
+    y = xb * inv.unsqueeze(-1)
+    qs = (torch.sign(y) * torch.floor(y.abs() + 0.5)).to(torch.int8)
+    out = torch.empty(*x.shape[:-1], D // QK8_0, Q8_0_BLOCK, dtype=torch.uint8, device=x.device)
+    out[..., :2] = d.half().unsqueeze(-1).view(torch.uint8).reshape(*d.shape, 2)
+    out[..., 2:] = qs.view(torch.uint8)
+    return out.reshape(*x.shape[:-1], D // QK8_0 * Q8_0_BLOCK)
