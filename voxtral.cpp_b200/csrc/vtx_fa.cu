@@ -21,11 +21,13 @@
 #include <atomic>
 #include <mutex>
 #include <utility>
+#include <vector>
 
 #include "../../include/vtx_fa.h"
 #include "vtx_ptx.cuh"
 #include "fa_splitkv.cuh"
 #include "fa_prefill_sm100.cuh"
+#include "fa_encoder_sk.cuh"
 #include "fa_decode_mma.cuh"
 #include "fa_decode_q8.cuh"
 #include "kv_append.cuh"
@@ -239,6 +241,69 @@ PrefillPlan plan_prefill(const Geo &g, const vtx_tensor *q, const vtx_tensor *k,
     p.n_cta_q = (p.n_tiles_q + p.nqt - 1) / p.nqt;
     if (p.convert) p.conv_bytes = 2 * align_up((size_t)g.Bkv * g.Hkv * g.n_kv * g.D * 2, 256);
     return p;
+}
+
+// Persistent encoder kernel (fa_encoder_sk.cuh): the bidirectional head_dim
+// 64 node with f16 Q / K / V read in place and no mask tensor, softcap or
+// causal flag -- the offline encoder (src/voxtral.cpp:1611) -- when its
+// per-pair grid would take more than one wave (several clips per call).  One
+// CTA per SM, each taking an equal share of the (Q-tile pair, key tile) work.  Workspace: a merge flag per
+// (CTA, Q tile), the producers' row maxima and sums, their partial O rows.
+struct SkPlan {
+    bool use = false;
+    int ctas = 0, n_pairs = 0, n_iter = 0;
+    int total = 0;
+    int bound[kSkMaxCtas + 1];
+    size_t flags_bytes = 0, part_bytes = 0;
+    size_t bytes() const { return use ? flags_bytes + part_bytes : 0; }
+};
+
+SkPlan plan_sk(const Geo &g, const PrefillPlan &pp, int q_type, int causal, float scale, float softcap, int sms) {
+    SkPlan p;
+    if (!pp.use || pp.convert || g.D != 64 || q_type != VTX_TYPE_F16 || g.kv_type != VTX_TYPE_F16) return p;
+    if (causal || softcap != 0.0f || !(scale > 0.0f) || pp.n_tiles_q < 2 || g.n_kv <= 0 || 128 % g.G) return p;
+    p.n_pairs = (pp.n_tiles_q + 1) / 2;
+    // One wave of per-pair CTAs (one clip of the offline encoder: 120 CTAs)
+    // runs faster on the per-pair kernel: a split pair's merge costs its
+    // owner ~2-4 us of memory round trips, about what the idle SMs would save
+    // (measured, 1500 x 1500 x 20 heads: 29.0 vs 23.9 us).  Beyond one wave
+    // the per-pair grid leaves a partial last wave, which this kernel avoids.
+    if ((long long)g.B * g.Hkv * p.n_pairs <= sms) return p;
+    p.n_iter = (g.n_kv + 127) / 128;
+    const long long total = (long long)g.B * g.Hkv * p.n_pairs * p.n_iter;
+    const long long ctas = std::min<long long>(std::min(sms, kSkMaxCtas), total / 4);
+    if (ctas < 1 || total > 0x7fffffffLL) return p;
+    p.total = (int)total;
+    p.ctas = (int)ctas;
+    p.flags_bytes = align_up((size_t)2 * p.ctas * sizeof(unsigned long long), 256);
+    p.part_bytes = align_up((size_t)2 * p.ctas * SkCfg<64>::PGROUPS * 128 * 4 * sizeof(float), 256);
+    p.use = true;
+    return p;
+}
+
+// Equal contiguous ranges, one per CTA.
+SkPlan plan_sk_ranges(const Geo &g, const PrefillPlan &pp, int q_type, int causal, float scale, float softcap,
+                      int sms) {
+    SkPlan p = plan_sk(g, pp, q_type, causal, scale, softcap, sms);
+    if (p.use)
+        for (int c = 0; c <= p.ctas; ++c) p.bound[c] = (int)((long long)c * p.total / p.ctas);
+    return p;
+}
+
+// Map of the persistent kernel's partials: F32 [groups][128 rows][4 floats]
+// (group = one column group of D/4 + 1 of one (CTA, Q tile)); one box of
+// 4 x 128 x (D/4 + 1) is a (CTA, Q tile)'s whole block.
+int encode_part_map(CUtensorMap *m, void *ptr, int blocks) {
+    if (!g_encode) return VTX_ERR_CUDA;
+    constexpr int PG = SkCfg<64>::PGROUPS;
+    cuuint64_t dims[3] = {4, 128, (cuuint64_t)blocks * PG};
+    cuuint64_t strides[2] = {16, 128 * 16};
+    cuuint32_t box[3] = {4, 128, PG};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, ptr, dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_WORKSPACE;
 }
 
 // ---- realtime encoder chunk geometry (host) -------------------------------------
@@ -592,13 +657,46 @@ int launch_prefill(int D, int nqt, bool hm, const CUtensorMap &mk, const CUtenso
                     : launch_prefill_d<128, 1>(hm, uf, mk, mv, mo, mq, a, grid, st);
 }
 
-size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, int sms) {
+// The mask is not part of the workspace query, so a shape the persistent
+// encoder kernel could take is sized for it; with a mask the per-pair kernel
+// runs and needs less.
+size_t workspace_for(const Geo &g, const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v,
+                     const vtx_fa_params *p, int sms) {
     if (g.n_q == 0) return 0;
     const PrefillPlan pp = plan_prefill(g, q, k, v, sms, false);   // the tile split does not change the workspace
-    if (pp.use) return pp.conv_bytes;
+    if (pp.use)
+        return std::max(pp.conv_bytes,
+                        plan_sk(g, pp, q->type, p->causal, p->scale, p->logit_softcap, sms).bytes());
     return plan_split(g, sms, g.n_kv, false).part_bytes;
 }
 
+int launch_encoder_sk(const SkPlan &sp, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mq,
+                      const CUtensorMap &mo, const PrefillArgs &a, void *workspace, cudaStream_t st) {
+    using C = SkCfg<64>;
+    static std::atomic<int> attr_done[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(fa_encoder_sk_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    char *ws = static_cast<char *>(workspace);
+    SkArgs sk{};
+    sk.n_pairs = sp.n_pairs;
+    sk.n_iter = sp.n_iter;
+    sk.total = sp.total;
+    std::memcpy(sk.bound, sp.bound, sizeof(int) * (sp.ctas + 1));
+    sk.flags = reinterpret_cast<unsigned long long *>(ws);
+    float *part = reinterpret_cast<float *>(ws + sp.flags_bytes);
+    sk.part = part;
+    CUtensorMap mp;
+    const int rc = encode_part_map(&mp, part, 2 * sp.ctas);
+    if (rc != VTX_OK) return rc;
+    return launch_pdl(fa_encoder_sk_kernel<64>, dim3((unsigned)sp.ctas), dim3(C::NTHREADS), C::SMEM, st, mk, mv, mq,
+                      mo, mp, a, sk);
+}
 
 // The batched ragged decode shared by vtx_flash_attn_decode_batched (scratch =
 // the caller's workspace) and vtx_flash_attn_decode_batched_noalloc (scratch =
@@ -696,7 +794,7 @@ size_t vtx_flash_attn_ext_workspace(const vtx_tensor *q, const vtx_tensor *k, co
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaGetLastError();
-    return workspace_for(g, q, k, v, sms);
+    return workspace_for(g, q, k, v, params, sms);
 }
 
 int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v, const vtx_tensor *mask,
@@ -714,7 +812,7 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
     if (rc != VTX_OK) return rc;
     if (g.n_q == 0 || g.B == 0 || g.Hq == 0) return VTX_OK;
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    if (workspace_bytes < workspace_for(g, q, k, v, ds->sms)) return VTX_ERR_WORKSPACE;
+    if (workspace_bytes < workspace_for(g, q, k, v, params, ds->sms)) return VTX_ERR_WORKSPACE;
     if (workspace && reinterpret_cast<uintptr_t>(workspace) % 256) return VTX_ERR_WORKSPACE;
 
     float qk_scale, softcap, m0, m1;
@@ -779,6 +877,14 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         a.q_tma = q->type == VTX_TYPE_F16 && !a.q_quant8 &&
                   encode_q_map(&mq, q->data, g.D, g.Hq, g.n_q, g.B, q->nb[1], q->nb[2], q->nb[3], g.G,
                                pp.tok_per_tile) == VTX_OK;
+        if (!mask && a.q_tma && a.o_tma) {
+            const SkPlan sp =
+                plan_sk_ranges(g, pp, q->type, params->causal, params->scale, params->logit_softcap, ds->sms);
+            if (sp.use) {
+                if (!workspace) return VTX_ERR_WORKSPACE;
+                return launch_encoder_sk(sp, mk, mv, mq, mo, a, workspace, st);
+            }
+        }
         if ((long long)pp.n_cta_q * g.Hkv > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
         // causal launches without a mask tensor or softcap, windowed or of more
         // than one wave, run the causal instantiation; beyond one wave its CTAs
