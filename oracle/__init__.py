@@ -366,20 +366,22 @@ ATOL, RTOL = 2e-3, 1e-2          # BASELINE north_star tolerance (fp32 accumulat
 def parity_verdict(got: np.ndarray, ggml: np.ndarray, fp64: np.ndarray) -> dict:
     """Judges a device result against the oracle run in both modes.
 
-    * vs fp64 truth: |got - fp64| <= ATOL + RTOL |fp64| everywhere.
-    * vs ggml mode:  |got - ggml| <= ATOL + RTOL |ggml| + |ggml - fp64|.
-      ggml's CPU kernel accumulates P.V in half precision when V is F16
-      (VKQ16), so over thousands of keys its own result drifts from exact
-      arithmetic by up to a few 1e-3 -- above ATOL.  A device that
-      accumulates in fp32 then differs from ggml by ggml's own rounding; the
-      bound admits exactly that per-element drift and nothing more.  For
-      F32 / Q8_0 V (f32 accumulator in ggml) the drift term is ~1e-6.
+    drift = |ggml - fp64| per element: how far ggml's own CPU arithmetic is
+    from exact attention.  It is large in two places: ggml accumulates P.V
+    in half precision when V is F16 (VKQ16), which over thousands of keys
+    moves the result by up to a few 1e-3; and for a Q8_0 K ggml quantises Q
+    to Q8_0 before the dot product, which the device reproduces on purpose.
+    The device result must be within ATOL + RTOL |ref| + drift of BOTH:
+      * ggml mode (it may differ from ggml by no more than ggml's own
+        rounding beyond the tolerance), and
+      * fp64 truth (it may be as far from exact as ggml is, no further).
+    Where ggml is exact (drift ~ 0) this is the plain tolerance twice.
     Returns the maxima and the verdict."""
     got = got.astype(np.float64)
     g = ggml.astype(np.float64)
     f = fp64.astype(np.float64)
     e_g, e_f, drift = np.abs(got - g), np.abs(got - f), np.abs(g - f)
-    ok_f = bool(np.all(e_f <= ATOL + RTOL * np.abs(f)))
+    ok_f = bool(np.all(e_f <= ATOL + RTOL * np.abs(f) + drift))
     ok_g = bool(np.all(e_g <= ATOL + RTOL * np.abs(g) + drift))
     return {"max_abs_err_vs_ggml": float(e_g.max()) if e_g.size else 0.0,
             "max_abs_err_vs_fp64": float(e_f.max()) if e_f.size else 0.0,

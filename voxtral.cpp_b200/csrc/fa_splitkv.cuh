@@ -442,10 +442,9 @@ fa_combine_kernel(const SplitArgs a, int gy)
 {
     grid_dep_wait();
     grid_dep_launch();
-    constexpr int C4 = D / 4, NSG = NT / C4, NW = NT / 32;   // float4 columns, split groups, warps
-    __shared__ float red_m[NW], red_l[NW];
+    constexpr int C4 = D / 4, NSG = NT / C4;                   // float4 columns, split groups
     __shared__ float4 acc_s[NSG][C4];
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int tid = threadIdx.x;
     const long long row_id = blockIdx.x;
     const int rows = a.tok_per_cta * a.hc;
     const int r = (int)(row_id % rows);
@@ -464,61 +463,64 @@ fa_combine_kernel(const SplitArgs a, int gy)
     const float *ml = a.part_ml + (w0 * MAXR + r) * 2;             // split s at ml[s * MAXR * 2]
     const float *po0 = a.part_o + (w0 * MAXR + r) * D;             // split s at po0[s * MAXR * D]
 
-    float M = -INFINITY;
-    for (int s = tid; s < nsp; s += NT) M = fmaxf(M, ml[(long long)s * MAXR * 2]);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
-    if (lane == 0) red_m[warp] = M;
-    __syncthreads();
-#pragma unroll
-    for (int w = 0; w < NW; ++w) M = fmaxf(M, red_m[w]);
-    const float Mu = M == -INFINITY ? 0.0f : M;
-
-    float L = 0.0f;
-    for (int s = tid; s < nsp; s += NT) {
-        const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
-        L += l == 0.0f ? 0.0f : l * ex2(m - Mu);
-    }
+    // One load round: thread (split group sg, float4 column c) merges the
+    // splits sg, sg + NSG, ... online (its own running max, four splits'
+    // loads in flight), then the groups are merged in shared memory in group
+    // order -- the same order on every run.
+    __shared__ float grp_m[NSG], grp_l[NSG];
     const int c = tid % C4, sg = tid / C4;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m_t = -INFINITY, l_t = 0.0f;
+    auto fold = [&](float m, float l, const float4 &x) {
+        if (l == 0.0f) return;                                 // a split with no key (or an empty row)
+        if (m > m_t) {
+            const float f = m_t == -INFINITY ? 0.0f : ex2(m_t - m);
+            acc.x *= f; acc.y *= f; acc.z *= f; acc.w *= f;
+            l_t *= f;
+            m_t = m;
+        }
+        const float w = ex2(m - m_t);
+        acc.x = fmaf(w, x.x, acc.x); acc.y = fmaf(w, x.y, acc.y);
+        acc.z = fmaf(w, x.z, acc.z); acc.w = fmaf(w, x.w, acc.w);
+        l_t = fmaf(w, l, l_t);
+    };
     int s = sg;
-    for (; s + 3 * NSG < nsp; s += 4 * NSG) {                   // four splits' loads in flight per thread
-        float f[4];
+    for (; s + 3 * NSG < nsp; s += 4 * NSG) {
+        float2 mlu[4];
         float4 x[4];
 #pragma unroll
         for (int u = 0; u < 4; ++u) {
             const long long su = s + u * NSG;
-            const float m = ml[su * MAXR * 2], l = ml[su * MAXR * 2 + 1];
-            f[u] = l == 0.0f ? 0.0f : ex2(m - Mu);
+            mlu[u] = *reinterpret_cast<const float2 *>(ml + su * MAXR * 2);
             x[u] = reinterpret_cast<const float4 *>(po0 + su * MAXR * D)[c];
         }
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
-            acc.x = fmaf(f[u], x[u].x, acc.x); acc.y = fmaf(f[u], x[u].y, acc.y);
-            acc.z = fmaf(f[u], x[u].z, acc.z); acc.w = fmaf(f[u], x[u].w, acc.w);
-        }
+        for (int u = 0; u < 4; ++u) fold(mlu[u].x, mlu[u].y, x[u]);
     }
     for (; s < nsp; s += NSG) {
-        const float m = ml[(long long)s * MAXR * 2], l = ml[(long long)s * MAXR * 2 + 1];
-        const float f = l == 0.0f ? 0.0f : ex2(m - Mu);
-        const float4 x = reinterpret_cast<const float4 *>(po0 + (long long)s * MAXR * D)[c];
-        acc.x = fmaf(f, x.x, acc.x); acc.y = fmaf(f, x.y, acc.y);
-        acc.z = fmaf(f, x.z, acc.z); acc.w = fmaf(f, x.w, acc.w);
+        const float2 m2 = *reinterpret_cast<const float2 *>(ml + (long long)s * MAXR * 2);
+        fold(m2.x, m2.y, reinterpret_cast<const float4 *>(po0 + (long long)s * MAXR * D)[c]);
     }
     acc_s[sg][c] = acc;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
-    if (lane == 0) red_l[warp] = L;
+    if (c == 0) {
+        grp_m[sg] = m_t;
+        grp_l[sg] = l_t;
+    }
     __syncthreads();
     if (tid < C4) {
-        L = 0.0f;
+        float M = -INFINITY;
 #pragma unroll
-        for (int w = 0; w < NW; ++w) L += red_l[w];
-        float4 o = acc_s[0][tid];
+        for (int q = 0; q < NSG; ++q) M = fmaxf(M, grp_m[q]);
+        float L = 0.0f;
+        float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int q = 1; q < NSG; ++q) {
+        for (int q = 0; q < NSG; ++q) {
+            if (grp_l[q] == 0.0f) continue;
+            const float w = ex2(grp_m[q] - M);
             const float4 v = acc_s[q][tid];
-            o.x += v.x; o.y += v.y; o.z += v.z; o.w += v.w;
+            o.x = fmaf(w, v.x, o.x); o.y = fmaf(w, v.y, o.y);
+            o.z = fmaf(w, v.z, o.z); o.w = fmaf(w, v.w, o.w);
+            L = fmaf(w, grp_l[q], L);
         }
         const float inv = L == 0.0f ? 0.0f : 1.0f / L;
         float *out = reinterpret_cast<float *>(a.dst + (long long)tok * a.d_nb2 + (long long)h * a.d_nb1 +
