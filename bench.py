@@ -46,6 +46,9 @@ ENC_TRAFFIC_BYTES = 11_590_656          # one encoder launch, dram read + write,
 DEC_TRAFFIC_RATIO_F16 = (1_058_088_000 + 7_246_080) / 1_057_517_568   # (read + write) / KV bytes, 32 streams
 DEC_TRAFFIC_RATIO_Q8 = (562_400_768 + 6_991_872) / 561_806_208     # (read + write) / KV bytes, 32 streams
 METRIC_DEC = "KV GB/s (decode)"
+CPU_PORT_NOTE = ("The port is scalar C with per-element f16 conversions: it has ggml-cpu's numerics, not its "
+                 "F16C/AVX-512 vector kernels, so it is slower than the reference's real --gpu none path and a "
+                 "GPU/CPU ratio against it overstates the speed-up.")
 
 
 def load_peaks():
@@ -320,7 +323,7 @@ def cpu_baseline_encoder(budget_s: float = 12.0):
     flops = 4.0 * D * H * n * n * layers
     return {"value": round(flops / spent / 1e12, 6), "unit": "TFLOP/s", "cores": cores, "kind": "port",
             "sample": f"{layers} of the 32 encoder layers of one configs[1] clip (1500 x 1500 x 20 heads x 64 each), "
-                      f"ggml-mode oracle on {cores} threads, {spent:.1f} s"}
+                      f"ggml-mode oracle on {cores} threads, {spent:.1f} s. " + CPU_PORT_NOTE}
 
 
 # ---- decode workload ---------------------------------------------------------------
@@ -797,23 +800,226 @@ def run_realtime(args, rank, world, local):
             "clocks": clocks.summary()}
 
 
+# ---- one decode call of the decoder node, batch 1 ---------------------
+def run_cfg0(args, rank, world, local):
+    """the decode node of src/voxtral.cpp:1802 as ggml builds it
+    (vtx_flash_attn_ext, n_q = 1): 32/8 heads x 128, 1024 keys, Q F32, K/V
+    f16 rows of a [kv_dim = 1024, n_ctx] cache, scale 1/sqrt(128), no mask.
+    GB/s over 64 rotating caches (268 MB > L2) replayed from a CUDA graph,
+    the single call's device time in that graph, and its host-to-completion
+    latency issued eagerly (median of 50)."""
+    import numpy as np
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    Hq, Hkv, D, n = 32, 8, 128, 1024
+    NB = 64
+    g = torch.Generator(device=dev)
+    g.manual_seed(707 + rank)
+    kc = torch.randn((NB, n, Hkv, D), generator=g, device=dev).to(torch.float16)
+    vc = torch.randn((NB, n, Hkv, D), generator=g, device=dev).to(torch.float16)
+    q = torch.randn((NB, 1, Hq, D), generator=g, device=dev)
+    out = torch.empty((NB, 1, 1, Hq, D), device=dev)
+    view = lambda t: t.permute(1, 0, 2).unsqueeze(0)             # (n, H, D) -> (1, H, n, D)
+    scale = D ** -0.5
+    ws = torch.empty(max(1, vtx_attn.workspace_bytes(view(q[0]), view(kc[0]), view(vc[0]), scale)),
+                     dtype=torch.uint8, device=dev)
+    stream = torch.cuda.Stream(device=dev)
+
+    def call(i):
+        vtx_attn.flash_attn_ext(view(q[i]), view(kc[i]), view(vc[i]), None, scale, out=out[i], workspace=ws,
+                                stream=stream)
+
+    with torch.cuda.stream(stream):
+        for i in range(NB):
+            call(i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=stream):
+        for i in range(NB):
+            call(i)
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(stream):
+        e0.record(stream)
+        for _ in range(20):
+            graph.replay()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    us_graph = e0.elapsed_time(e1) / (20 * NB) * 1e3
+    lat = []
+    for i in range(50):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        call(i % NB)
+        stream.synchronize()
+        lat.append((time.perf_counter() - t0) * 1e6)
+    kv_bytes = 2 * n * Hkv * D * 2
+    peaks = load_peaks()
+    res = {"workload": "configs[0] decode call: n_q 1, 32/8 heads x 128, 1024 keys, Q F32, K/V f16 cache rows",
+           "us_per_call_graph": round(us_graph, 2), "us_per_call_eager_median": round(float(np.median(lat)), 2),
+           "kv_GBps_rotating": round(kv_bytes / (us_graph * 1e-6) / 1e9, 1),
+           "hbm_frac": round(kv_bytes / (us_graph * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+           "l2": f"{NB} rotating caches ({NB * kv_bytes / 1e6:.0f} MB > L2)"}
+    if rank == 0 and not getattr(args, "no_check", False):
+        import oracle as O
+        qn, kn, vn = q[0].cpu().numpy(), kc[0].cpu().numpy(), vc[0].cpu().numpy()
+        vw = lambda a: a.transpose(1, 0, 2)[None]
+        v = O.parity_verdict(out[0].cpu().numpy(), O.flash_attn_ext(vw(qn), vw(kn), vw(vn), None, scale),
+                             O.flash_attn_ext(vw(qn), vw(kn), vw(vn), None, scale, mode=O.MODE_FP64))
+        res["parity"] = {k: v[k] for k in ("max_abs_err_vs_ggml", "max_abs_err_vs_fp64", "ok")}
+    return res
+
+
+# ---- multi-GPU: configs[4] streams sharded by LPT, long prefill split by KV head ------
+def run_decode_sharded(args, rank, world, local, kv="f16"):
+    """configs[4]'s 256 ragged streams (the same streams at every N) placed on
+    the ranks by LPT bin packing on kv_len (shard.lpt_shard); each rank decodes
+    its streams (one layer per step), no collective on the data path.  Strong
+    scaling: streams/sec = 256 / (max over ranks of the step time)."""
+    import numpy as np
+    import torch
+    import shard
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    S, Hq, Hkv, D = DEC["n_seq"], DEC["Hq"], DEC["Hkv"], DEC["D"]
+    q8 = kv == "q8_0"
+    row = D // 32 * 34 if q8 else D * 2
+    lens = np.random.default_rng(4321).integers(DEC["lo"], DEC["hi"] + 1, S).astype(np.int32)
+    mine = shard.lpt_shard(lens.tolist(), world)[rank]
+    ks, vs = [], []
+    for i in mine:                                      # per-stream seeds: the same data at every N
+        g = torch.Generator(device=dev)
+        g.manual_seed(10_000 + int(i))
+        x = torch.randn((int(lens[i]), Hkv, D), generator=g, device=dev)
+        y = torch.randn((int(lens[i]), Hkv, D), generator=g, device=dev)
+        ks.append(vtx_attn.quantize_q8_0(x) if q8 else x.half())
+        vs.append(vtx_attn.quantize_q8_0(y) if q8 else y.half())
+    ml = lens[mine]
+    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(ml).to(dev), Hq, Hkv, D,
+                                    vtx_attn.Q8_0 if q8 else vtx_attn.F16, Hkv * row, row, int(lens.max()),
+                                    1.0 / D ** 0.5)
+    q = torch.randn((len(mine), Hq, D), device=dev)
+    out = torch.empty_like(q)
+    stream = torch.cuda.Stream(device=dev)
+    with torch.cuda.stream(stream):
+        for _ in range(3):
+            plan(q, out, stream)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = max(3, min(args.steps, 10))
+    barrier(world)
+    e0.record(stream)
+    for _ in range(steps):
+        plan(q, out, stream)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = barrier_max(e0.elapsed_time(e1) / steps, world)
+    kv_total = float(lens.astype(np.int64).sum()) * Hkv * row * 2
+    mine_bytes = barrier_max(float(ml.astype(np.int64).sum()) * Hkv * row * 2, world)
+    return {"workload": f"configs[4] 256 streams, {kv} KV, one layer per step, LPT-sharded over {world} GPU(s)",
+            "scaling": "strong", "ms_per_step": round(ms, 4), "streams_per_sec": round(S / (ms * 1e-3), 1),
+            "kv_GBps_aggregate": round(kv_total / (ms * 1e-3) / 1e9, 1),
+            "max_rank_share": round(mine_bytes / kv_total, 4), "streams_on_rank0": len(mine)}
+
+
+def run_prefill_head_split(args, rank, world, local):
+    """Long-context prefill (8192 tokens, causal GQA 32/8 x 128, f16 Q/K/V)
+    split by KV head over the ranks (shard.head_split_prefill: each rank's
+    heads straight into its block of the gather buffer, one in-place NCCL
+    all-gather).  Reports the step time, aggregate TFLOP/s and the share of
+    the step the all-gather adds over the rank's attention alone."""
+    import torch
+    import vtx_attn
+
+    dev = torch.device("cuda", local)
+    n, Hq, Hkv, D = 8192, 32, 8, 128
+    g = torch.Generator(device=dev)
+    g.manual_seed(818)                                  # the same problem on every rank
+    qkv = torch.randn((3, n, Hq, D), generator=g, device=dev).to(torch.float16)
+    q = qkv[0].permute(1, 0, 2).unsqueeze(0)
+    k = qkv[1, :, :Hkv].permute(1, 0, 2).unsqueeze(0)
+    v = qkv[2, :, :Hkv].permute(1, 0, 2).unsqueeze(0)
+    scale = D ** -0.5
+    per = Hkv // world
+    G = Hq // Hkv
+    qs, ks_, vs_ = q[:, rank * per * G:(rank + 1) * per * G], k[:, rank * per:(rank + 1) * per], \
+        v[:, rank * per:(rank + 1) * per]
+    out_local = torch.empty((1, n, per * G, D), device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def attn_only():
+        vtx_attn.flash_attn_ext(qs, ks_, vs_, None, scale, causal=True, out=out_local)
+
+    def step():
+        if world == 1:
+            return vtx_attn.flash_attn_ext(q, k, v, None, scale, causal=True)
+        import shard
+        return shard.head_split_prefill(q, k, v, None, scale, causal=True)
+
+    def timed(fn, reps):
+        for _ in range(2):
+            fn()
+        torch.cuda.synchronize()
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        return barrier_max(e0.elapsed_time(e1) / reps, world)
+
+    reps = max(3, min(args.steps, 10))
+    ms_step = timed(step, reps)
+    ms_attn = timed(attn_only, reps)
+    flop = 4.0 * D * Hq * (n * (n + 1) // 2)
+    return {"workload": f"8192-token causal prefill, GQA 32/8 x 128, f16, KV heads split over {world} GPU(s)",
+            "scaling": "strong", "ms_per_step": round(ms_step, 4), "tflops_aggregate": round(flop / (ms_step * 1e-3) / 1e12, 1),
+            "ms_attention_only": round(ms_attn, 4),
+            "allgather_share": round(max(0.0, 1.0 - ms_attn / ms_step), 4) if world > 1 else 0.0}
+
+
 # ---- reference arm ------------------------------------------------------------------
 def run_reference(args):
+    """The reference arm: the CPU restatement of ggml's flash_attn_ext (the
+    oracle, ggml mode) on the configs[1] encoder layer, every host core, rank
+    0 only.  One step = one encoder layer (1500 x 1500 x 20 heads x 64, a
+    bounded sample of the 32-layer clip); the same --steps / --warmup as the
+    vtx arm."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return None
+    import numpy as np
     import oracle as O
     O.build()
-    vals = []
-    for _ in range(max(0, min(args.warmup, 1))):
-        cpu_baseline_encoder(budget_s=1.0)
-    for _ in range(max(1, min(args.steps, 3))):
-        vals.append(cpu_baseline_encoder(budget_s=8.0))
-    v = sorted(x["value"] for x in vals)[len(vals) // 2]
-    cb = dict(vals[0])
-    cb["value"] = v
+    n, H, D = ENC["n"], ENC["H"], ENC["D"]
+    rng = np.random.default_rng(5)
+    view = lambda a: a.transpose(1, 0, 2)[None]
+    cores = O.n_cores()
+    layer = [rng.standard_normal((n, H, D)).astype(np.float16) for _ in range(3)]
+
+    def one_layer():
+        t0 = time.perf_counter()
+        O.flash_attn_ext(view(layer[0]), view(layer[1]), view(layer[2]), None, D ** -0.5, threads=cores)
+        return time.perf_counter() - t0
+
+    for _ in range(args.warmup):
+        one_layer()
+    spent = sum(one_layer() for _ in range(args.steps))
+    v = round(4.0 * D * H * n * n * args.steps / spent / 1e12, 6)
+    cb = {"value": v, "unit": "TFLOP/s", "cores": cores, "kind": "port",
+          "sample": f"{args.steps} configs[1] encoder layers (1500 x 1500 x 20 heads x 64), {spent:.1f} s on "
+                    f"{cores} threads. " + CPU_PORT_NOTE}
     return {"impl": "reference", "metric": METRIC_ENC, "value": v, "unit": "TFLOP/s",
-            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": len(vals), "warmup": args.warmup,
+            "n_gpus": int(os.environ.get("WORLD_SIZE", "1")), "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(spent / args.steps * 1e3, 3),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic N(0,1) f16 Q/K/V (BASELINE configs[1] shapes)",
             "config": {"workload": "configs[1] audio-encoder self-attention, 30 s clip: 1500 frames, 20 heads x 64, "
@@ -834,6 +1040,8 @@ def main():
                     choices=["encoder", "decode", "kv_append", "decode_step", "realtime", "prefill"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the oracle check of the timed outputs")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="encoder workload: skip the other configs' sub-measurements")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
     ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="decode workload: KV cache type")
@@ -864,6 +1072,27 @@ def main():
                 res[key] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "roofline", "config",
                                               "data", "parity")}
                 torch.cuda.empty_cache()
+        if not args.no_extra:
+            # the other BASELINE configs, each timed on its own after the
+            # headline (sub-objects; at N > 1 every rank runs its own copy,
+            # except the two sharded measurements, which split one problem)
+            import copy
+            xargs = copy.copy(args)
+            xargs.steps, xargs.warmup = 5, 3
+            res["cfg0_decode_call"] = run_cfg0(xargs, rank, world, local)
+            pre = run_prefill(xargs, rank, world, local)
+            res["cfg2_prefill"] = {k: pre[k] for k in ("metric", "value", "unit", "roofline", "detail")}
+            ds = run_decode_step(xargs, rank, world, local)
+            res["decode_step_batch1"] = {k: ds[k] for k in ("metric", "unit", "detail")}
+            xargs.steps, xargs.warmup = 1, 1
+            rt = run_realtime(xargs, rank, world, local)
+            res["cfg3_realtime"] = {k: rt[k] for k in ("metric", "value", "unit", "ms_per_step", "detail", "config")}
+            torch.cuda.empty_cache()
+            xargs.steps = 5
+            res["cfg4_decode_sharded"] = {kv: run_decode_sharded(xargs, rank, world, local, kv)
+                                          for kv in ("f16", "q8_0")}
+            torch.cuda.empty_cache()
+            res["prefill_head_split"] = run_prefill_head_split(xargs, rank, world, local)
         if rank == 0 and world == 1 and not args.no_cpu_baseline:
             res["cpu_baseline"] = cpu_baseline_encoder()
     else:

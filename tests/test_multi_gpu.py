@@ -38,7 +38,7 @@ def _worker(rank, world, port, case, result_path):
         # the spawned rank receives copies of the case's views (pickling drops the
         # shared buffers), so they go to the device as contiguous tensors
         q, k, v = (torch.from_numpy(np.ascontiguousarray(a)).cuda(rank) for a in (case.q, case.k, case.v))
-        out = shard.head_split_prefill(q, k, v, None, case.scale, causal=bool(case.causal))
+        out = shard.as_heads(shard.head_split_prefill(q, k, v, None, case.scale, causal=bool(case.causal)))
         torch.cuda.synchronize()
         torch.save(out.cpu(), f"{result_path}.{rank}")
     finally:

@@ -57,7 +57,7 @@ def _worker(rank, world, port, q, k, v, mask, scale, kw, result_path):
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        out = shard.head_split_prefill(q, k, v, mask, scale, attn=_oracle_attn, **kw)
+        out = shard.as_heads(shard.head_split_prefill(q, k, v, mask, scale, attn=_oracle_attn, **kw))
         torch.save(out, f"{result_path}.{rank}")
     finally:
         dist.destroy_process_group()

@@ -10,8 +10,8 @@ src/voxtral.cpp:2409, :2451 keep static thread_local graph state).  On an
   KV bytes per decode step; encoder clips are simply dealt round robin.
 * Long-context prefill split by KV head (``head_split_prefill``): rank r owns
   KV heads [r*Hkv/N, (r+1)*Hkv/N) and the Hq/Hkv query heads of each, runs the
-  attention node on its slice, and one all-gather assembles ggml's
-  [Dv, Hq, n_q, B] result.  All remote bytes move through the collective into
+  attention node on its slice straight into its block of the gather buffer,
+  and one in-place all-gather assembles ggml's [Dv, Hq, n_q, B] result.  All remote bytes move through the collective into
   local memory; no kernel reads a peer's memory.
 
 The attention callable is injected (default: vtx_attn.flash_attn_ext) so the
@@ -56,14 +56,21 @@ def head_split_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: 
     """Attention over KV heads split across the ranks of ``group``.
 
     q: (B, Hq, n_q, D), k/v: (B, Hkv, n_kv, D) — the full views; each rank
-    slices out its heads (views, no copy).  Returns the full (B, n_q, Hq, Dv)
-    result on every rank (ggml's permuted dst), assembled with one
-    all_gather_into_tensor of the per-rank (B, n_q, Hq/N, Dv) slices."""
+    slices out its heads (views, no copy).  Rank r computes query heads
+    [r*Hq/N, (r+1)*Hq/N) straight into block r of one buffer
+    (N, B, n_q, Hq/N, Dv) -- the attention writes ggml's strides, so there is
+    no copy -- and one in-place all_gather_into_tensor fills the other blocks.
+    Returns the buffer as a view (B, n_q, N, Hq/N, Dv): ggml's
+    [Dv, Hq, n_q, B] result with the head axis split at rank boundaries
+    (head = r * Hq/N + j), every rank holding all of it.  A consumer that
+    takes strides (vtx_attn_out_proj's A operand) reads it as is;
+    ``as_heads`` makes the contiguous (B, n_q, Hq, Dv) copy."""
     import torch.distributed as dist
     if float(kw.get("max_bias", 0.0)) != 0.0:
         # ggml's ALiBi slope depends on the global head index; each rank's
         # call numbers its heads from 0, so slopes would be wrong past rank 0
         raise ValueError("head_split_prefill does not support max_bias != 0 (ALiBi)")
+    direct = attn is None
     if attn is None:
         import vtx_attn
         attn = vtx_attn.flash_attn_ext
@@ -78,11 +85,20 @@ def head_split_prefill(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, mask: 
     ms = mask
     if mask is not None and mask.dim() == 4 and mask.shape[1] == Hq:
         ms = mask[:, hr.start * G:hr.stop * G]
-    part = attn(qs, ks, vs, ms, scale, **kw)                     # (B, n_q, Hq/N, Dv)
-    part = part.contiguous()
-    Dv = part.shape[-1]
-    # output concatenated along dim 0 (the layout every backend accepts)
-    gathered = torch.empty((world * B,) + tuple(part.shape[1:]), dtype=part.dtype, device=part.device)
-    dist.all_gather_into_tensor(gathered, part, group=group)
-    # (N*B, n_q, Hq/N, Dv) -> (N, B, n_q, Hq/N, Dv) -> (B, n_q, N, Hq/N, Dv) -> (B, n_q, Hq, Dv)
-    return gathered.view((world,) + tuple(part.shape)).permute(1, 2, 0, 3, 4).reshape(B, n_q, Hq, Dv)
+    Dv = v.shape[-1] if v.dtype != torch.uint8 else v.shape[-1] // 34 * 32
+    # blocks concatenated along dim 0, the layout every backend's all-gather takes
+    buf = torch.empty((world * B, n_q, Hq // world, Dv), dtype=torch.float32, device=q.device)
+    mine = buf[rank * B:(rank + 1) * B]
+    if direct:
+        attn(qs, ks, vs, ms, scale, out=mine, **kw)              # written in place, ggml strides
+    else:
+        mine.copy_(attn(qs, ks, vs, ms, scale, **kw))
+    dist.all_gather_into_tensor(buf, mine, group=group)           # in place: rank r's block is the input
+    return buf.view(world, B, n_q, Hq // world, Dv).permute(1, 2, 0, 3, 4)
+
+
+def as_heads(x: torch.Tensor) -> torch.Tensor:
+    """(B, n_q, N, Hq/N, Dv) result of head_split_prefill -> contiguous
+    (B, n_q, Hq, Dv) (ggml's dst layout); a copy when N > 1."""
+    B, n_q, N, h, Dv = x.shape
+    return x.reshape(B, n_q, N * h, Dv)
