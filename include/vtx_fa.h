@@ -280,6 +280,41 @@ VTX_API int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t s
                                size_t dst_row_bytes, size_t row_bytes, const vtx_enc_chunk *chunks,
                                int32_t n_chunks, void *stream);
 
+/* ---- attention output projection ------------------------------------------ */
+
+/* The output projection that consumes each attention node's result:
+ *     attn_out  = ggml_cont(attn_out); reshape to [Dv*Hq, n]
+ *     attn_proj = ggml_mul_mat(attn_o_weight, attn_out)     // [dim, n]
+ *     attn_proj = ggml_add(attn_proj, attn_o_bias)          // encoder only
+ *     x         = ggml_add(residual, attn_proj)
+ * (src/voxtral.cpp:1612-1617 encoder, src/voxtral.cpp:1804-1809 decoder) as
+ * one tcgen05 GEMM: dst[t][n] = residual[t][n] + bias[n]
+ *                              + sum_k f16(attn[t][k]) * w[n][k]
+ * with f32 accumulation (ggml rounds the activations to f16 for an F16
+ * weight).  The attention output is read in place -- no contiguous copy --
+ * from the layout vtx_flash_attn_ext writes (heads at attn->nb[1], tokens
+ * at attn->nb[2]), or, with head_block = h > 0, from heads stored in blocks
+ * of h at a stride of block_nb bytes (head i = block i / h, head i % h in
+ * it): the rank-major result of a KV-head-split prefill after its
+ * all-gather.
+ *   attn     F32 [Dv, Hq, n, 1], Dv a multiple of 64
+ *   w        F16 [K = Dv * Hq, N] (ggml's weight: row r = output feature r)
+ *   bias     optional F32 [N]
+ *   residual optional F32 [N, n]; may be dst itself
+ *   dst      F32 [N, n]
+ * Asynchronous on `stream`; no allocation, no workspace. */
+typedef struct vtx_out_proj_args {
+    const vtx_tensor *attn;
+    int32_t head_block;          /* 0: one head stride; h > 0: blocks of h heads */
+    int32_t reserved;
+    size_t block_nb;             /* byte stride between head blocks (head_block > 0) */
+    const vtx_tensor *w;
+    const vtx_tensor *bias;
+    const vtx_tensor *residual;
+    vtx_tensor *dst;
+} vtx_out_proj_args;
+VTX_API int vtx_attn_out_proj(const vtx_out_proj_args *args, void *stream);
+
 /* Diagnostic: synchronises `stream`, returns and clears the device-side error
  * word of the current device (0 = none).  Kernels set it instead of hanging
  * when a bounded pipeline wait runs out, or when a batched-decode stream base

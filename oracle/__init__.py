@@ -97,6 +97,8 @@ def lib():
         L.vtx_ref_kv_append.argtypes = [ctypes.c_int] * 5 + [ctypes.c_float] + [vp] * 8 + [ctypes.c_size_t,
                                                                                           ctypes.c_int]
         L.vtx_ref_kv_append.restype = ctypes.c_int
+        L.vtx_ref_out_proj.argtypes = [vp, i64, vp, i64, vp, vp, i64, vp, i64] + [ctypes.c_int] * 5
+        L.vtx_ref_out_proj.restype = ctypes.c_int
         _lib = L
     return _lib
 
@@ -356,6 +358,27 @@ def encoder_stitch(chunk_out: np.ndarray, chunks, n_rows: int) -> np.ndarray:
     out = np.zeros((n_rows,) + chunk_out.shape[2:], dtype=chunk_out.dtype)
     for c, ch in enumerate(chunks):
         out[ch["write_offset"]:ch["write_offset"] + ch["stride"]] = chunk_out[c, ch["skip"]:ch["skip"] + ch["stride"]]
+    return out
+
+
+def out_proj(attn: np.ndarray, w: np.ndarray, bias: np.ndarray | None = None, residual: np.ndarray | None = None,
+             mode: int = MODE_GGML, threads: int | None = None) -> np.ndarray:
+    """Host version of vtx_attn_out_proj: attn (n, K) F32 (the attention
+    output with its heads flattened, ggml's [Dv*Hq, n]), w (N, K) float16,
+    bias (N,) F32 or None, residual (n, N) F32 or None -> (n, N) F32."""
+    a = np.ascontiguousarray(attn, dtype=np.float32)
+    wh = np.ascontiguousarray(w, dtype=np.float16)
+    n, K = a.shape
+    N = wh.shape[0]
+    assert wh.shape[1] == K
+    b = np.ascontiguousarray(bias, dtype=np.float32) if bias is not None else None
+    r = np.ascontiguousarray(residual, dtype=np.float32) if residual is not None else None
+    out = np.empty((n, N), dtype=np.float32)
+    rc = lib().vtx_ref_out_proj(a.ctypes.data, K, wh.ctypes.data, K, b.ctypes.data if b is not None else None,
+                                r.ctypes.data if r is not None else None, N, out.ctypes.data, N, n, K, N, mode,
+                                threads or n_cores())
+    if rc != 0:
+        raise ValueError(f"oracle rejected operands: status {rc}")
     return out
 
 

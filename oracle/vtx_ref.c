@@ -515,3 +515,78 @@ int vtx_ref_kv_append(int n_tokens, int n_head_q, int n_head_kv, int head_dim, i
     free(tmp);
     return 0;
 }
+
+/* ---- attention output projection ----------------------------------------
+ * dst[t][n] = residual[t][n] + bias[n] + sum_k A[t][k] * W[n][k]: the
+ * ggml_mul_mat(attn_o_weight, attn_out) (+ attn_o_bias) + residual add after
+ * each attention node (src/voxtral.cpp:1612-1617 encoder, :1804-1809
+ * decoder).  ggml mode: ggml's CPU mul_mat for an F16 weight converts the F32
+ * activations to its vec_dot type, F16 (round to nearest even), and
+ * accumulates the F16 x F16 products in f32 (ggml_vec_dot_f16); the bias and
+ * residual adds are f32.  fp64 mode: A unrounded, everything in double.
+ * A: n rows of K floats at a stride of lda floats; W: N rows of K halves at
+ * ldw; residual / dst: n rows of N floats at ldr / ldd (residual may be
+ * NULL, and may equal dst); bias: N floats or NULL.  Rows are spread over
+ * n_threads. */
+typedef struct {
+    const float *A; int64_t lda;
+    const uint16_t *W; int64_t ldw;
+    const float *bias, *res; int64_t ldr;
+    float *dst; int64_t ldd;
+    int n, K, N, mode;
+    atomic_long next;
+} proj_job_t;
+
+static void *proj_worker(void *arg)
+{
+    proj_job_t *J = (proj_job_t *)arg;
+    float *a16 = malloc(sizeof(float) * (size_t)J->K);
+    if (!a16) return NULL;
+    for (;;) {
+        const long t = atomic_fetch_add(&J->next, 1);
+        if (t >= J->n) break;
+        const float *a = J->A + t * J->lda;
+        for (int k = 0; k < J->K; k++) a16[k] = J->mode == VTX_REF_FP64 ? a[k] : h2f(f2h(a[k]));
+        for (int o = 0; o < J->N; o++) {
+            const uint16_t *w = J->W + (int64_t)o * J->ldw;
+            double y;
+            if (J->mode == VTX_REF_FP64) {
+                double s = 0.0;
+                for (int k = 0; k < J->K; k++) s += (double)a16[k] * (double)h2f(w[k]);
+                y = s;
+            } else {
+                float s = 0.0f;
+                for (int k = 0; k < J->K; k++) s += a16[k] * h2f(w[k]);
+                y = s;
+            }
+            if (J->mode == VTX_REF_FP64) {
+                if (J->bias) y += J->bias[o];
+                if (J->res) y += J->res[t * J->ldr + o];
+                J->dst[t * J->ldd + o] = (float)y;
+            } else {
+                float yf = (float)y;
+                if (J->bias) yf += J->bias[o];
+                if (J->res) yf = J->res[t * J->ldr + o] + yf;
+                J->dst[t * J->ldd + o] = yf;
+            }
+        }
+    }
+    free(a16);
+    return NULL;
+}
+
+int vtx_ref_out_proj(const float *A, int64_t lda, const uint16_t *W, int64_t ldw, const float *bias,
+                     const float *res, int64_t ldr, float *dst, int64_t ldd, int n, int K, int N, int mode,
+                     int n_threads)
+{
+    if (!A || !W || !dst || n < 0 || K <= 0 || N <= 0) return VTX_ERR_SHAPE;
+    proj_job_t J = {A, lda, W, ldw, bias, res, ldr, dst, ldd, n, K, N, mode, 0};
+    if (n_threads < 1) n_threads = 1;
+    if (n_threads > 256) n_threads = 256;
+    if (n < n_threads) n_threads = n > 0 ? n : 1;
+    pthread_t th[256];
+    for (int t = 1; t < n_threads; t++) pthread_create(&th[t], NULL, proj_worker, &J);
+    proj_worker(&J);
+    for (int t = 1; t < n_threads; t++) pthread_join(th[t], NULL);
+    return 0;
+}

@@ -30,7 +30,7 @@ def test_header_declares_the_entry_points():
     assert {"vtx_flash_attn_ext", "vtx_flash_attn_ext_workspace", "vtx_flash_attn_decode_batched",
             "vtx_flash_attn_decode_batched_workspace", "vtx_strerror", "vtx_abi_version",
             "vtx_read_device_error", "vtx_flash_attn_decode_batched_noalloc", "vtx_kv_append",
-            "vtx_decode_advance", "vtx_encoder_chunk_plan", "vtx_encoder_stitch"} <= syms
+            "vtx_decode_advance", "vtx_encoder_chunk_plan", "vtx_encoder_stitch", "vtx_attn_out_proj"} <= syms
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -148,3 +148,35 @@ def test_workspace_query_is_host_only(lib):
     n = lib.vtx_flash_attn_ext_workspace(ctypes.byref(q), ctypes.byref(k), ctypes.byref(k),
                                          ctypes.byref(V.params(0.088)))
     assert 0 < n < (1 << 30)
+
+
+def test_out_proj_args_layout(tmp_path):
+    import vtx_attn
+    src = tmp_path / "probe_op.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vtx_fa.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu\\n", sizeof(vtx_out_proj_args),'
+                   ' offsetof(vtx_out_proj_args, block_nb), offsetof(vtx_out_proj_args, w),'
+                   ' offsetof(vtx_out_proj_args, residual), offsetof(vtx_out_proj_args, dst));'
+                   ' return 0;}\n')
+    exe = tmp_path / "probe_op"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    A = vtx_attn.OutProjArgs
+    assert vals == [ctypes.sizeof(A), A.block_nb.offset, A.w.offset, A.residual.offset, A.dst.offset]
+
+
+def test_out_proj_validation_without_device(lib):
+    """Shape and type errors come back before any device work."""
+    import vtx_attn
+    a = vtx_attn._raw_tensor(vtx_attn.F32, [64, 4, 10, 1], [4, 256, 1024, 10240], 0x1000)
+    w = vtx_attn._raw_tensor(vtx_attn.F16, [256, 128, 1, 1], [2, 512], 0x1000)
+    y = vtx_attn._raw_tensor(vtx_attn.F32, [128, 10, 1, 1], [4, 512], 0x1000)
+    args = vtx_attn.OutProjArgs()
+    args.attn, args.w, args.dst = ctypes.addressof(a), ctypes.addressof(w), ctypes.addressof(y)
+    wbad = vtx_attn._raw_tensor(vtx_attn.F16, [200, 128, 1, 1], [2, 400], 0x1000)     # K != Dv * Hq
+    args.w = ctypes.addressof(wbad)
+    assert lib.vtx_attn_out_proj(ctypes.byref(args), None) == -3
+    wf32 = vtx_attn._raw_tensor(vtx_attn.F32, [256, 128, 1, 1], [4, 1024], 0x1000)
+    args.w = ctypes.addressof(wf32)
+    assert lib.vtx_attn_out_proj(ctypes.byref(args), None) == -2
+    assert lib.vtx_attn_out_proj(None, None) == -1

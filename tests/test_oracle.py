@@ -154,3 +154,19 @@ def test_parity_verdict_admits_ggml_drift_only():
     far = f.copy()
     far[10] -= 6e-3                                 # the other way from ggml, beyond its drift + ATOL
     assert not O.parity_verdict(far, g, f)["ok"]
+
+
+def test_oracle_out_proj_fp64_is_exact_matmul():
+    """The out-projection restatement: fp64 mode equals a float64 matmul plus
+    bias and residual; ggml mode differs only by rounding the activations to
+    f16 (ggml's vec_dot type for an F16 weight)."""
+    rng = np.random.default_rng(21)
+    a = rng.standard_normal((9, 256)).astype(np.float32)
+    w = (rng.standard_normal((130, 256)) / 16).astype(np.float16)
+    b = rng.standard_normal(130).astype(np.float32)
+    r = rng.standard_normal((9, 130)).astype(np.float32)
+    ref = a.astype(np.float64) @ w.astype(np.float64).T + b + r
+    assert np.abs(O.out_proj(a, w, b, r, mode=O.MODE_FP64) - ref).max() < 1e-5
+    a16 = a.astype(np.float16).astype(np.float64)
+    ref16 = a16 @ w.astype(np.float64).T + b + r
+    assert np.abs(O.out_proj(a, w, b, r) - ref16).max() < 1e-4

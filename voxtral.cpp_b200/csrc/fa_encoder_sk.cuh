@@ -143,8 +143,6 @@ __device__ __forceinline__ void tma_store_3d(const void *desc, const void *src, 
                  "r"(smem_u32(src)), "r"(x), "r"(y), "r"(z)
                  : "memory");
 }
-// every committed bulk store has completed (its writes are performed)
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 __device__ __forceinline__ void fence_proxy_async_global() {
     asm volatile("fence.proxy.async.global;" ::: "memory");
 }
@@ -587,7 +585,7 @@ fa_encoder_sk_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_const
                     if (!good) break;
                     if (producer) {
                         // the partial is in memory: release it to the owner
-                        bulk_wait_all();
+                        bulk_wait_all_done();
                         fence_proxy_async_global();
                         __threadfence();
 #pragma unroll
@@ -598,7 +596,7 @@ fa_encoder_sk_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_const
 #pragma unroll
                     for (int t = 0; t < NQT; ++t) mbar_arrive(&stage_free[t]);
                 }
-                bulk_wait_all();
+                bulk_wait_all_done();
             }
         }
     }

@@ -32,6 +32,7 @@
 #include "fa_decode_q8.cuh"
 #include "kv_append.cuh"
 #include "enc_stitch.cuh"
+#include "out_proj.cuh"
 
 using namespace vtx;
 
@@ -1090,6 +1091,101 @@ int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t src_row_b
         if (r != VTX_OK) return VTX_ERR_CUDA;
     }
     return VTX_OK;
+}
+
+int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
+    if (!p || !p->attn || !p->w || !p->dst) return VTX_ERR_NULL;
+    const vtx_tensor &A = *p->attn, &W = *p->w, &Y = *p->dst;
+    if (A.type != VTX_TYPE_F32 || W.type != VTX_TYPE_F16 || Y.type != VTX_TYPE_F32) return VTX_ERR_TYPE;
+    const int64_t Dv = A.ne[0], Hq = A.ne[1], n = A.ne[2];
+    if (A.ne[3] != 1 || Dv <= 0 || Dv % 64 || Hq <= 0 || n < 0) return VTX_ERR_SHAPE;
+    const int64_t K = Dv * Hq, N = W.ne[1];
+    if (W.ne[0] != K || W.ne[2] != 1 || W.ne[3] != 1 || N <= 0) return VTX_ERR_SHAPE;
+    if (Y.ne[0] != N || Y.ne[1] != n || Y.ne[2] != 1 || Y.ne[3] != 1) return VTX_ERR_SHAPE;
+    if (K > INT32_MAX || N > INT32_MAX || n > INT32_MAX) return VTX_ERR_SHAPE;
+    if (n == 0) return VTX_OK;
+    if (!A.data || !W.data || !Y.data) return VTX_ERR_NULL;
+    const int hb = p->head_block > 0 ? p->head_block : (int)Hq;
+    if (Hq % hb) return VTX_ERR_SHAPE;
+    const int h_out = (int)(Hq / hb);
+    if (A.nb[0] != 4 || W.nb[0] != 2 || Y.nb[0] != 4) return VTX_ERR_STRIDE;
+    const size_t outer = h_out > 1 ? p->block_nb : A.nb[1] * (size_t)hb;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(A.data) | reinterpret_cast<uintptr_t>(W.data) |
+                         reinterpret_cast<uintptr_t>(Y.data) | (uintptr_t)A.nb[1] | (uintptr_t)A.nb[2] |
+                         (uintptr_t)outer | (uintptr_t)W.nb[1] | (uintptr_t)Y.nb[1];
+    if (al % 16) return VTX_ERR_STRIDE;
+    const float *bias = nullptr;
+    if (p->bias) {
+        if (p->bias->type != VTX_TYPE_F32 || p->bias->ne[0] != N || p->bias->nb[0] != 4) return VTX_ERR_SHAPE;
+        bias = static_cast<const float *>(p->bias->data);
+        if (!bias) return VTX_ERR_NULL;
+    }
+    const char *res = nullptr;
+    long long res_nb1 = 0;
+    if (p->residual) {
+        const vtx_tensor &R = *p->residual;
+        if (R.type != VTX_TYPE_F32 || R.ne[0] != N || R.ne[1] != n || R.nb[0] != 4) return VTX_ERR_SHAPE;
+        res = static_cast<const char *>(R.data);
+        res_nb1 = (long long)R.nb[1];
+        if (!res) return VTX_ERR_NULL;
+        if ((reinterpret_cast<uintptr_t>(res) | (uintptr_t)res_nb1) % 16) return VTX_ERR_STRIDE;
+    }
+    DeviceState *ds = nullptr;
+    int rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    if (!g_encode) return VTX_ERR_CUDA;
+    CUtensorMap ma, mw, my;
+    {
+        // A: [Dv, heads in a block, tokens, blocks], one box = 64 columns of one head x 128 tokens
+        cuuint64_t dims[4] = {(cuuint64_t)Dv, (cuuint64_t)hb, (cuuint64_t)n, (cuuint64_t)h_out};
+        cuuint64_t strides[3] = {(cuuint64_t)(hb > 1 ? A.nb[1] : Dv * 4), (cuuint64_t)(n > 1 ? A.nb[2] : 16),
+                                 (cuuint64_t)outer};
+        for (int i = 0; i < 3; ++i)
+            if (strides[i] == 0 || strides[i] % 16 || strides[i] >= (1ULL << 40)) return VTX_ERR_STRIDE;
+        cuuint32_t box[4] = {64, 1, 128, 1}, estr[4] = {1, 1, 1, 1};
+        if (g_encode(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A.data, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return VTX_ERR_STRIDE;
+    }
+    {
+        cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)N};
+        cuuint64_t strides[1] = {(cuuint64_t)W.nb[1]};
+        cuuint32_t box[2] = {64, 128}, estr[2] = {1, 1};
+        if (g_encode(&mw, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, W.data, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return VTX_ERR_STRIDE;
+    }
+    // the output and the residual: F32 [N, n], boxes of 32 columns x 128 tokens, 128-byte swizzle
+    auto rows_map = [&](CUtensorMap *m, void *ptr, size_t nb1) {
+        cuuint64_t dims[2] = {(cuuint64_t)N, (cuuint64_t)n};
+        cuuint64_t strides[1] = {(cuuint64_t)(n > 1 ? nb1 : (size_t)((N * 4 + 15) / 16 * 16))};
+        cuuint32_t box[2] = {32, 128}, estr[2] = {1, 1};
+        return g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, ptr, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    };
+    CUtensorMap mr;
+    std::memset(&mr, 0, sizeof(mr));
+    if (!rows_map(&my, Y.data, Y.nb[1])) return VTX_ERR_STRIDE;
+    if (res && !rows_map(&mr, const_cast<char *>(res), (size_t)res_nb1)) return VTX_ERR_STRIDE;
+    static std::atomic<int> attr_done[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(out_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OutProjCfg::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    OutProjArgs a{};
+    a.M = (int)n; a.N = (int)N; a.K = (int)K; a.Dv = (int)Dv; a.h_in = hb;
+    a.bias = bias; a.res = res; a.res_nb1 = res_nb1; a.err = ds->err;
+    const dim3 grid((unsigned)((n + OutProjCfg::BM - 1) / OutProjCfg::BM), (unsigned)((N + OutProjCfg::BN - 1) / OutProjCfg::BN));
+    if (grid.y > 65535) return VTX_ERR_UNSUPPORTED;
+    return launch_pdl(out_proj_kernel, grid, dim3(OutProjCfg::NTHREADS), OutProjCfg::SMEM,
+                      static_cast<cudaStream_t>(stream), ma, mw, my, mr, a);
 }
 
 int vtx_read_device_error(void *stream) {

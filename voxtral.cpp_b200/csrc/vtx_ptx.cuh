@@ -113,6 +113,28 @@ __device__ __forceinline__ void tma_store_4d(const void *desc, const void *src, 
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // wait until every committed bulk store has finished READING shared memory
 __device__ __forceinline__ void bulk_wait_read_all() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// ... until at most N committed groups are still reading shared memory
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory"); }
+// every committed bulk store has completed (its writes are performed)
+__device__ __forceinline__ void bulk_wait_all_done() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// 2-D tiled load (x innermost; x * element size a multiple of 16 bytes).
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *desc, uint64_t *bar, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cta.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+        "l"(desc), "r"(smem_u32(bar)), "r"(x), "r"(y)
+        : "memory");
+}
+// 2-D tiled store shared -> global (bulk async group); x * element size a
+// multiple of 16 bytes, no negative coordinate; boxes past the tensor's
+// extent are clipped.
+__device__ __forceinline__ void tma_store_2d_f32(const void *desc, const void *src, int x, int y) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(desc),
+                 "r"(smem_u32(src)), "r"(x), "r"(y)
+                 : "memory");
+}
 
 // ---- tcgen05: TMEM ----------------------------------------------------------
 // Allocate `ncols` TMEM columns (power of two >= 32); the base address is

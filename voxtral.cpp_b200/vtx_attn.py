@@ -71,6 +71,13 @@ class KvAppendArgs(ctypes.Structure):
                 ("cache_nb1", ctypes.c_size_t), ("reserved", ctypes.c_int32 * 4)]
 
 
+class OutProjArgs(ctypes.Structure):
+    """vtx_out_proj_args (include/vtx_fa.h)."""
+    _fields_ = [("attn", ctypes.c_void_p), ("head_block", ctypes.c_int32), ("reserved", ctypes.c_int32),
+                ("block_nb", ctypes.c_size_t), ("w", ctypes.c_void_p), ("bias", ctypes.c_void_p),
+                ("residual", ctypes.c_void_p), ("dst", ctypes.c_void_p)]
+
+
 class EncChunk(ctypes.Structure):
     """vtx_enc_chunk (include/vtx_fa.h): one chunk of the realtime encoder run."""
     _fields_ = [("mel_offset", ctypes.c_int32), ("mel_frames", ctypes.c_int32), ("n_tokens", ctypes.c_int32),
@@ -122,6 +129,8 @@ def load(path: str = LIB_PATH):
                                      ctypes.c_size_t, ctypes.c_size_t, P(EncChunk), ctypes.c_int32,
                                      ctypes.c_void_p]
     L.vtx_encoder_stitch.restype = ctypes.c_int
+    L.vtx_attn_out_proj.argtypes = [P(OutProjArgs), ctypes.c_void_p]
+    L.vtx_attn_out_proj.restype = ctypes.c_int
     _lib = L
     return L
 
@@ -380,3 +389,60 @@ def quantize_q8_0(x: torch.Tensor) -> torch.Tensor:
     out[..., :2] = d.half().unsqueeze(-1).view(torch.uint8).reshape(*d.shape, 2)
     out[..., 2:] = qs.view(torch.uint8)
     return out.reshape(*x.shape[:-1], D // QK8_0 * Q8_0_BLOCK)
+
+
+def _raw_tensor(ttype: int, ne, nb, ptr: int) -> VtxTensor:
+    d = VtxTensor()
+    d.type = ttype
+    for i in range(4):
+        d.ne[i] = ne[i] if i < len(ne) else 1
+        d.nb[i] = nb[i] if i < len(nb) else (d.nb[i - 1] * d.ne[i - 1])
+    d.data = ptr
+    return d
+
+
+def out_proj(attn: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None,
+             residual: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+             stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+    """vtx_attn_out_proj: out = residual + bias + f16(attn) @ w^T (f32 accumulate),
+    the output projection after the attention node (src/voxtral.cpp:1612-1617,
+    :1804-1809).  attn: (1, n, Hq, Dv) float32 as flash_attn_ext returns it,
+    any strides, read in place; or (1, n, R, h, Dv), the rank-major result of
+    shard.head_split_prefill (head = r * h + j).  w: (N, Hq * Dv) float16;
+    bias: (N,) float32 or None; residual: (n, N) float32 or None (it may be
+    `out`).  Returns out (n, N) float32."""
+    if attn.dtype != torch.float32 or w.dtype != torch.float16:
+        raise VtxError(-2, "attn must be float32 and w float16")
+    es = 4
+    if attn.dim() == 4:
+        _, n, Hq, Dv = attn.shape
+        head_nb, tok_nb = attn.stride(2) * es, attn.stride(1) * es
+        head_block, block_nb = 0, 0
+    elif attn.dim() == 5:
+        _, n, R, h, Dv = attn.shape
+        Hq = R * h
+        head_nb, tok_nb = attn.stride(3) * es, attn.stride(1) * es
+        head_block, block_nb = h, attn.stride(2) * es
+    else:
+        raise VtxError(-3, "attn must be (1, n, Hq, Dv) or (1, n, R, h, Dv)")
+    if attn.shape[0] != 1 or attn.stride(-1) != 1:
+        raise VtxError(-3, "one batch, unit-stride head dim")
+    N, K = w.shape
+    if out is None:
+        out = torch.empty((n, N), dtype=torch.float32, device=attn.device)
+    a = _raw_tensor(F32, [Dv, Hq, n, 1], [4, head_nb, tok_nb, tok_nb * n], attn.data_ptr())
+    wd = _raw_tensor(F16, [K, N, 1, 1], [2, w.stride(0) * 2], w.data_ptr())
+    yd = _raw_tensor(F32, [N, n, 1, 1], [4, out.stride(0) * 4], out.data_ptr())
+    bd = _raw_tensor(F32, [N, 1, 1, 1], [4], bias.data_ptr()) if bias is not None else None
+    rd = _raw_tensor(F32, [N, n, 1, 1], [4, residual.stride(0) * 4], residual.data_ptr()) \
+        if residual is not None else None
+    args = OutProjArgs()
+    args.attn = ctypes.addressof(a)
+    args.head_block, args.block_nb = head_block, block_nb
+    args.w = ctypes.addressof(wd)
+    args.bias = ctypes.addressof(bd) if bd is not None else None
+    args.residual = ctypes.addressof(rd) if rd is not None else None
+    args.dst = ctypes.addressof(yd)
+    s = stream if stream is not None else torch.cuda.current_stream(attn.device)
+    _check(load().vtx_attn_out_proj(ctypes.byref(args), ctypes.c_void_p(s.cuda_stream)), "vtx_attn_out_proj")
+    return out
