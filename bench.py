@@ -327,11 +327,12 @@ def cpu_baseline_encoder(budget_s: float = 12.0):
 
 
 # ---- decode workload ---------------------------------------------------------------
-def make_decode_inputs(S: int, q8: bool, seed_np: int, seed_dev: int, dev):
+def make_decode_inputs(S: int, q8, seed_np: int, seed_dev: int, dev):
     """configs[4] inputs: S streams with kv_len ~ U[512, 16384] (numpy seed),
     per stream a K and a V cache of kv_len rows x 8 KV heads x 128 drawn
-    N(0,1) on the device (torch seed), stored f16 or quantized to Q8_0 by
-    ggml's rule; Q (S, 32, 128) F32 N(0,1)."""
+    N(0,1) on the device (torch seed), stored f16, quantized to Q8_0 by
+    ggml's rule (q8 True or "q8_0"), or F32 as the reference keeps it
+    (q8 = "f32"); Q (S, 32, 128) F32 N(0,1)."""
     import numpy as np
     import torch
     import vtx_attn
@@ -343,6 +344,8 @@ def make_decode_inputs(S: int, q8: bool, seed_np: int, seed_dev: int, dev):
 
     def cache(L):
         x = torch.randn((int(L), Hkv, D), generator=g, device=dev)
+        if q8 == "f32":
+            return x
         return vtx_attn.quantize_q8_0(x) if q8 else x.to(torch.float16)
 
     ks = [cache(L) for L in lens]
@@ -351,7 +354,7 @@ def make_decode_inputs(S: int, q8: bool, seed_np: int, seed_dev: int, dev):
     return lens, ks, vs, q
 
 
-def check_decode_rows(q, ks, vs, lens, out, q8: bool, n_check: int = 8, seed: int = 0):
+def check_decode_rows(q, ks, vs, lens, out, q8, n_check: int = 8, seed: int = 0):
     """Checker (outside every timed region): the oracle's ggml-mode batched
     decode on a seeded sample of n_check streams against the device output
     rows of the same streams, judged by oracle.parity_verdict (fp64 truth
@@ -359,11 +362,14 @@ def check_decode_rows(q, ks, vs, lens, out, q8: bool, n_check: int = 8, seed: in
     import numpy as np
     import oracle as O
     Hkv, D = DEC["Hkv"], DEC["D"]
-    row = D // 32 * 34 if q8 else D * 2
+    f32 = q8 == "f32"
+    q8 = q8 is True or q8 == "q8_0"
+    row = D // 32 * 34 if q8 else D * (4 if f32 else 2)
     idx = sorted(np.random.default_rng(seed).choice(len(lens), size=min(n_check, len(lens)), replace=False).tolist())
     kl = [ks[i].cpu().numpy() for i in idx]
     vl = [vs[i].cpu().numpy() for i in idx]
-    args = (q[idx].cpu().numpy(), kl, vl, lens[idx], 1.0 / D ** 0.5, O.Q8_0 if q8 else O.F16, Hkv, Hkv * row, row)
+    args = (q[idx].cpu().numpy(), kl, vl, lens[idx], 1.0 / D ** 0.5, O.Q8_0 if q8 else O.F32 if f32 else O.F16, Hkv,
+            Hkv * row, row)
     ref = O.decode_batched(*args)
     truth = O.decode_batched(*args, mode=O.MODE_FP64)
     v = O.parity_verdict(out[idx].cpu().numpy(), ref, truth)
@@ -394,12 +400,14 @@ def run_decode(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     S, Hq, Hkv, D = args.streams, DEC["Hq"], DEC["Hkv"], DEC["D"]
-    q8 = getattr(args, "kv", "f16") == "q8_0"
-    row = D // 32 * 34 if q8 else D * 2                   # bytes of one head's K (or V) row
-    lens, ks, vs, q = make_decode_inputs(S, q8, 4321 + rank, 77 + rank, dev)
-    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D,
-                                    vtx_attn.Q8_0 if q8 else vtx_attn.F16, Hkv * row, row, int(lens.max()),
-                                    1.0 / D ** 0.5)
+    kvname = getattr(args, "kv", "f16")
+    q8 = kvname == "q8_0"
+    f32 = kvname == "f32"
+    row = D // 32 * 34 if q8 else D * (4 if f32 else 2)   # bytes of one head's K (or V) row
+    lens, ks, vs, q = make_decode_inputs(S, "f32" if f32 else q8, 4321 + rank, 77 + rank, dev)
+    kvt = vtx_attn.Q8_0 if q8 else vtx_attn.F32 if f32 else vtx_attn.F16
+    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D, kvt, Hkv * row, row,
+                                    int(lens.max()), 1.0 / D ** 0.5)
     out = torch.empty_like(q)
     stream = torch.cuda.Stream(device=dev)
     with torch.cuda.stream(stream):
@@ -421,18 +429,18 @@ def run_decode(args, rank, world, local):
     value = kv_bytes * args.steps * world / (ms * 1e-3) / 1e9
     peaks = load_peaks()
     achieved = kv_bytes / (ms_local / args.steps * 1e-3) / 1e9
-    parity = check_decode_rows(q, ks, vs, lens, out, q8) if (rank == 0 and not getattr(args, "no_check", False)) \
-        else None
+    parity = check_decode_rows(q, ks, vs, lens, out, kvname) \
+        if (rank == 0 and not getattr(args, "no_check", False)) else None
     return {
         "parity": parity,
         "metric": METRIC_DEC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q8_0" if q8 else "f16",
+        "scaling": "weak", "vs_baseline": None, "dtype": kvname,
         "data": ("synthetic N(0,1) KV quantized to Q8_0 by ggml's rule (quantize_row_q8_0_ref)" if q8
-                 else "synthetic N(0,1) f16 KV")
+                 else f"synthetic N(0,1) {kvname} KV")
                 + ", ragged lengths U[512,16384] seeded per rank",
         "config": {"workload": f"configs[4] batched decode: {S} streams, GQA 32/8 x 128, "
-                               f"{'Q8_0' if q8 else 'f16'} KV, 1 layer per step",
+                               f"{kvname.upper()} KV, 1 layer per step",
                    "l2": f"inputs larger than L2 ({kv_bytes / 1e9:.1f} GB KV per step)",
                    "parallelism": f"dp{world} (independent streams per GPU)"},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"], "unit": "GB/s",
@@ -1117,7 +1125,7 @@ def main():
                     help="encoder workload: skip the other configs' sub-measurements")
     ap.add_argument("--no-decode", action="store_true", help="encoder workload: skip the decode sub-measurement")
     ap.add_argument("--streams", type=int, default=DEC["n_seq"], help="decode workload: streams per GPU")
-    ap.add_argument("--kv", default="f16", choices=["f16", "q8_0"], help="decode workload: KV cache type")
+    ap.add_argument("--kv", default="f16", choices=["f16", "q8_0", "f32"], help="decode workload: KV cache type")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
 
@@ -1139,7 +1147,7 @@ def main():
             import copy
             dargs = copy.copy(args)
             dargs.steps, dargs.warmup = 5, 3
-            for kv, key in (("f16", "decode"), ("q8_0", "decode_q8_0")):
+            for kv, key in (("f16", "decode"), ("q8_0", "decode_q8_0"), ("f32", "decode_f32")):
                 dargs.kv = kv
                 d = run_decode(dargs, rank, world, local)
                 res[key] = {k: d[k] for k in ("metric", "value", "unit", "ms_per_step", "dtype", "roofline", "config",

@@ -69,24 +69,26 @@ def test_cfg1_encoder_as_benched():
         assert r["ok"], f"layer {l}: {r}"
 
 
-@pytest.mark.parametrize("kv", ["f16", "q8_0"])
+@pytest.mark.parametrize("kv", ["f16", "q8_0", "f32"])
 def test_cfg4_decode_full_shape(kv):
+    """configs[4] at its size, f16 and Q8_0 caches, and the reference's own
+    F32 cache (src/voxtral.cpp:1126-1136, f32 arithmetic as ggml's CPU kernel)."""
     import bench
     import vtx_attn
     dev = torch.device("cuda", 0)
     q8 = kv == "q8_0"
     Hq, Hkv, D = bench.DEC["Hq"], bench.DEC["Hkv"], bench.DEC["D"]
-    row = D // 32 * 34 if q8 else D * 2
-    lens, ks, vs, q = bench.make_decode_inputs(bench.DEC["n_seq"], q8, 4321, 77, dev)
+    row = D // 32 * 34 if q8 else D * (4 if kv == "f32" else 2)
+    lens, ks, vs, q = bench.make_decode_inputs(bench.DEC["n_seq"], "f32" if kv == "f32" else q8, 4321, 77, dev)
     assert lens.min() >= 512 and lens.max() <= 16384 and len(lens) == 256
-    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D,
-                                    vtx_attn.Q8_0 if q8 else vtx_attn.F16, Hkv * row, row, int(lens.max()),
-                                    1.0 / D ** 0.5)
+    kvt = {"f16": vtx_attn.F16, "q8_0": vtx_attn.Q8_0, "f32": vtx_attn.F32}[kv]
+    plan = vtx_attn.DecodeBatchPlan(ks, vs, torch.from_numpy(lens).to(dev), Hq, Hkv, D, kvt, Hkv * row, row,
+                                    int(lens.max()), 1.0 / D ** 0.5)
     out = torch.full_like(q, float("nan"))
     plan(q, out)
     torch.cuda.synchronize()
     assert torch.isfinite(out).all()
-    r = bench.check_decode_rows(q, ks, vs, lens, out, q8, n_check=12, seed=3)
+    r = bench.check_decode_rows(q, ks, vs, lens, out, kv, n_check=12, seed=3)
     assert r["ok"], f"{kv}: {r}"
 
 

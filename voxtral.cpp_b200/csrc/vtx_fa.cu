@@ -30,6 +30,7 @@
 #include "fa_encoder_sk.cuh"
 #include "fa_decode_mma.cuh"
 #include "fa_decode_q8.cuh"
+#include "fa_decode_f32.cuh"
 #include "kv_append.cuh"
 #include "enc_stitch.cuh"
 #include "out_proj.cuh"
@@ -535,6 +536,33 @@ int launch_decode_mma(const SplitArgs &a, int D, cudaStream_t st) {
     return D == 64 ? launch_decode_mma_t<64>(a, st) : launch_decode_mma_t<128>(a, st);
 }
 
+// Decode over an F32 cache on the f32 streaming kernel (the reference's own
+// cache type): n_q = 1, at most 4 query heads per KV head, 16-byte rows.
+template <int D>
+int launch_decode_f32_t(const SplitArgs &a, cudaStream_t st) {
+    using C = DecodeF32Cfg<D>;
+    static std::atomic<int> attr_done[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(fa_decode_f32_kernel<D>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    const long long items = (long long)a.B * a.Hkv * a.n_splits;
+    if ((items + C::WARPS - 1) / C::WARPS > 0x7fffffffLL) return VTX_ERR_UNSUPPORTED;
+    if (launch_pdl(fa_decode_f32_kernel<D>, dim3((unsigned)((items + C::WARPS - 1) / C::WARPS)), dim3(128), C::SMEM,
+                   st, a, (int)items) != VTX_OK)
+        return VTX_ERR_CUDA;
+    if (!a.write_final) return launch_combine<D, 4>(a, a.Hkv, st);
+    return VTX_OK;
+}
+
+int launch_decode_f32(const SplitArgs &a, int D, cudaStream_t st) {
+    return D == 64 ? launch_decode_f32_t<64>(a, st) : launch_decode_f32_t<128>(a, st);
+}
+
 // Q8_0 streaming decode: one CTA per (stream, group of hpc KV heads, key
 // split); the heads' slices of a token row are copied as one contiguous span,
 // so heads must be adjacent in the row (nb2 = one head's 136-byte row) and the
@@ -572,6 +600,10 @@ int launch_decode_q8(const SplitArgs &a, int hpc, cudaStream_t st) {
 
 bool decode_mma_ok(int kv_type, int n_q, int G, int vec, int maxr, int n_hchunks) {
     return kv_type == VTX_TYPE_F16 && n_q == 1 && G <= 4 && vec == 16 && maxr == 4 && n_hchunks == 1;
+}
+
+bool decode_f32_ok(int kv_type, int n_q, int G, int vec, int maxr, int n_hchunks) {
+    return kv_type == VTX_TYPE_F32 && n_q == 1 && G <= 4 && vec == 16 && maxr == 4 && n_hchunks == 1;
 }
 
 int launch_split(const SplitArgs &a, int D, int kvt, int maxr, dim3 grid, cudaStream_t st) {
@@ -614,9 +646,10 @@ bool batch_streaming(const vtx_decode_batch *b) {
     const int rb = row_bytes(b->kv_type, b->head_dim);
     const int vec =
         pick_vec(rb, {(unsigned long long)b->kv_nb1, (unsigned long long)(b->n_head_kv > 1 ? b->kv_nb2 : 0)});
-    // F16 only: a Q8_0 CTA covers all heads of a split with 211 KB of shared
-    // memory (one per SM), so its fixed cost needs the coarser default splits
-    return b->kv_type == VTX_TYPE_F16 && vec == 16;
+    // F16 and F32 (warp per item); a Q8_0 CTA covers all heads of a split with
+    // 211 KB of shared memory (one per SM), so its fixed cost needs the
+    // coarser default splits
+    return (b->kv_type == VTX_TYPE_F16 || b->kv_type == VTX_TYPE_F32) && vec == 16;
 }
 
 template <int D, int NQT, bool HM, bool UF, bool CSL = false>
@@ -757,6 +790,7 @@ int decode_batched_impl(const vtx_decode_batch *b, void *scratch, size_t scratch
     if (!a.vec) return VTX_ERR_STRIDE;
     a.err = ds->err;
     if (decode_mma_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks)) return launch_decode_mma(a, D, st);
+    if (decode_f32_ok(b->kv_type, 1, g.G, a.vec, sp.maxr, sp.n_hchunks)) return launch_decode_f32(a, D, st);
     if (const int hpc = decode_q8_hpc(b->kv_type, D, 1, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
                                       a.v_nb1, a.v_nb2))
         return launch_decode_q8(a, hpc, st);
@@ -936,6 +970,9 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
     if (decode_mma_ok(g.kv_type, g.n_q, g.G, a.vec, sp.maxr, sp.n_hchunks) && !mask && !params->causal &&
         params->logit_softcap == 0.0f)
         return launch_decode_mma(a, g.D, st);
+    if (decode_f32_ok(g.kv_type, g.n_q, g.G, a.vec, sp.maxr, sp.n_hchunks) && !mask && !params->causal &&
+        params->logit_softcap == 0.0f)
+        return launch_decode_f32(a, g.D, st);
     if (!mask && !params->causal && params->logit_softcap == 0.0f) {
         const int hpc = decode_q8_hpc(g.kv_type, g.D, g.n_q, g.G, g.Hkv, sp.maxr, sp.n_hchunks, a.k_nb1, a.k_nb2,
                                       a.v_nb1, a.v_nb2);
