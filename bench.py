@@ -576,8 +576,11 @@ def run_decode_step(args, rank, world, local):
 
     dev = torch.device("cuda", local)
     res = {}
-    for name, L, kvt, start in (("configs[2]", 30, vtx_attn.F16, 391), ("configs[3]", 26, vtx_attn.Q8_0, 7300)):
-        g = DecodeStepGraph(L, 1, DEC["Hq"], DEC["Hkv"], DEC["D"], kvt, 8192, [start], device=dev)
+    for name, L, kvt, start, fused in (("configs[2]", 30, vtx_attn.F16, 391, True),
+                                       ("configs[3]", 26, vtx_attn.Q8_0, 7300, True),
+                                       ("configs[2]_two_calls", 30, vtx_attn.F16, 391, False),
+                                       ("configs[3]_two_calls", 26, vtx_attn.Q8_0, 7300, False)):
+        g = DecodeStepGraph(L, 1, DEC["Hq"], DEC["Hkv"], DEC["D"], kvt, 8192, [start], device=dev, fused=fused)
         gen = torch.Generator(device=dev)
         gen.manual_seed(61 + rank)
         for l in range(L):                                   # prefill rows
@@ -608,6 +611,7 @@ def run_decode_step(args, rank, world, local):
         row = g.row
         step_bytes = L * kv * row * 2
         res[name] = {"layers": L, "kv_type": "q8_0" if kvt == vtx_attn.Q8_0 else "f16", "kv_len_at_end": kv,
+                     "launches_per_layer": 1 if fused else 3,
                      "us_per_token_graph": round(us, 1), "us_per_token_eager": round(us_eager, 1),
                      "us_per_layer_graph": round(us / L, 2), "kv_GBps_graph": round(step_bytes / (us * 1e-6) / 1e9, 1)}
         del g
@@ -619,9 +623,11 @@ def run_decode_step(args, rank, world, local):
             "scaling": "weak", "vs_baseline": None, "dtype": "f16",
             "data": "synthetic N(0,1) f32 Q/K/V projections, seeded",
             "config": {"workload": "batch-1 decode step, attention part of every layer: KV append (RoPE, ring "
-                                   "write) + decode attention, counters advanced on the device",
+                                   "write) + decode attention, counters advanced on the device; vtx_decode_layer "
+                                   "(one launch per layer), and the two-call path (append, attention + merge) "
+                                   "for comparison",
                        "parallelism": f"dp{world}"},
-            "detail": res, "peak_hbm_gbs": peaks["hbm_gbs"], "gpu_launches": 200 * (30 * 3 + 1)}
+            "detail": res, "peak_hbm_gbs": peaks["hbm_gbs"], "gpu_launches": 200 * (30 * 1 + 1)}
 
 
 # ---- decoder prefill (D = 128, causal GQA) ----------------------------
@@ -710,7 +716,8 @@ def run_realtime(args, rank, world, local):
                output that the reference stitches through host memory);
       decoder: 7500 tokens (one per 80 ms) over 26 layers, GQA 32/8 x 128,
                Q8_0 ring cache growing from 39 tokens: DecodeStepGraph replays
-               (KV append + decode attention per layer, device counters).
+               (one vtx_decode_layer launch per layer: RoPE, ring write,
+               decode attention; device counters).
     One step = the whole 10 minutes; value = audio-sec/sec = 600 x ranks /
     (max over ranks of the step time)."""
     import torch
@@ -804,7 +811,7 @@ def run_realtime(args, rank, world, local):
                        "decoder_ms": round(d_ms, 2), "decoder_us_per_token": round(d_ms * 1e3 / (n_tok - start), 1),
                        "decoder_kv_GBps": round(dec_bytes / (d_ms * 1e-3) / 1e9, 1), "chunks": C,
                        "enc_tokens": total},
-            "gpu_launches": args.steps * (L_enc + 1 + (n_tok - start) * (L_dec * 3 + 1)),
+            "gpu_launches": args.steps * (L_enc + 1 + (n_tok - start) * (L_dec + 1)),
             "clocks": clocks.summary()}
 
 

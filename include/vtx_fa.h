@@ -240,6 +240,57 @@ VTX_API int vtx_kv_append(const vtx_kv_append_args *args, void *stream);
 VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int32_t n, int32_t window,
                                void *stream);
 
+/* One decoder layer's attention for one new token per stream, in one launch:
+ * what vtx_kv_append (RoPE of Q and K, K/V into ring row slots[s]) followed by
+ * vtx_flash_attn_decode_batched computes, without the two dependent launches
+ * and the split-merge launch between them.  Replaces per layer and decoded
+ * token the ggml_rope_ext of Q and K and the ggml_cpy of K and V into the
+ * cache at kv_offset (src/voxtral.cpp:1744-1770) and the decode
+ * ggml_flash_attn_ext node (src/voxtral.cpp:1783-1805, n_tokens = 1,
+ * mask = NULL), inside run_decoder_step (:2438-2473).
+ * - q: [n_seq] rows of n_head_q * head_dim F32 (un-rotated; heads contiguous,
+ *   token stride q_nb1 bytes); k, v: [n_seq] rows of n_head_kv * head_dim.
+ * - The new K (rotated) and V are written to row slots[s] of the stream's
+ *   caches k_cache_ptrs[s] / v_cache_ptrs[s] (rows cache_nb1 bytes apart,
+ *   heads contiguous, F16 or Q8_0), then attention runs over rows
+ *   [0, kv_len[s]) with kv_len[s] counting the new row (slots[s] < kv_len[s]).
+ * - dst: [n_seq] rows of n_head_q * head_dim F32 (ggml's result for n_q = 1).
+ * - head_dim 128, n_head_q / n_head_kv <= 8; Q8_0 needs an even n_head_kv.
+ *   q, k, v, dst, the cache bases and every stride 16-byte aligned.
+ * - early = 1: the cache rows other than slots[s], kv_len, slots and the
+ *   pointer arrays may be read while the kernel launched just before still
+ *   runs (they must be complete before it); only q, k, v and positions are
+ *   waited for.  early = 0 reads nothing before that kernel completes.
+ * - workspace: vtx_decode_layer_workspace(args) bytes, 256-byte aligned:
+ *   split partials and one arrival counter per stream and KV head.  Zero it
+ *   once before the first call (cudaMemset); every completed call leaves it
+ *   zeroed again.  After a call that reported a device error
+ *   (vtx_read_device_error), zero it again.  Calls sharing a workspace must
+ *   not overlap on the GPU.
+ * Asynchronous on `stream`; no allocation, no host synchronisation. */
+typedef struct {
+    int32_t n_seq, n_head_q, n_head_kv, head_dim;
+    int32_t kv_type;                    /* VTX_TYPE_F16 or VTX_TYPE_Q8_0 */
+    int32_t max_kv_len;                 /* bound on every kv_len[s] (sizes the key splits) */
+    float freq_base;                    /* RoPE base (voxtral.cpp: 1e6) */
+    float scale;                        /* softmax scale, 1/sqrt(head_dim) */
+    const float *q; size_t q_nb1;
+    const float *k; size_t k_nb1;
+    const float *v; size_t v_nb1;
+    const int32_t *positions;           /* RoPE position of each stream's new token */
+    const int32_t *slots;               /* cache row the new token goes to */
+    const int32_t *kv_len;              /* rows attended, the new one included */
+    const void *const *k_cache_ptrs;    /* [n_seq] */
+    const void *const *v_cache_ptrs;
+    size_t cache_nb1;
+    float *dst; size_t dst_nb1;
+    int32_t early;
+    int32_t reserved[3];
+} vtx_decode_layer_args;
+VTX_API size_t vtx_decode_layer_workspace(const vtx_decode_layer_args *args);
+VTX_API int vtx_decode_layer(const vtx_decode_layer_args *args, void *workspace, size_t workspace_bytes,
+                             void *stream);
+
 /* ---- realtime encoder: chunk plan and device-side stitch ------------------ */
 
 /* One chunk of the realtime model's chunked encoder run (run_encoder_chunked,

@@ -30,7 +30,8 @@ def test_header_declares_the_entry_points():
     assert {"vtx_flash_attn_ext", "vtx_flash_attn_ext_workspace", "vtx_flash_attn_decode_batched",
             "vtx_flash_attn_decode_batched_workspace", "vtx_strerror", "vtx_abi_version",
             "vtx_read_device_error", "vtx_flash_attn_decode_batched_noalloc", "vtx_kv_append",
-            "vtx_decode_advance", "vtx_encoder_chunk_plan", "vtx_encoder_stitch", "vtx_attn_out_proj"} <= syms
+            "vtx_decode_advance", "vtx_encoder_chunk_plan", "vtx_encoder_stitch", "vtx_attn_out_proj",
+            "vtx_decode_layer", "vtx_decode_layer_workspace"} <= syms
 
 
 def test_library_exports_every_declared_symbol(lib):
@@ -180,3 +181,40 @@ def test_out_proj_validation_without_device(lib):
     args.w = ctypes.addressof(wf32)
     assert lib.vtx_attn_out_proj(ctypes.byref(args), None) == -2
     assert lib.vtx_attn_out_proj(None, None) == -1
+
+
+def test_decode_layer_args_layout(tmp_path):
+    import vtx_attn
+    src = tmp_path / "probe_dl.c"
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "vtx_fa.h"\n'
+                   'int main(void){printf("%zu %zu %zu %zu %zu %zu\\n", sizeof(vtx_decode_layer_args),'
+                   ' offsetof(vtx_decode_layer_args, q), offsetof(vtx_decode_layer_args, positions),'
+                   ' offsetof(vtx_decode_layer_args, k_cache_ptrs), offsetof(vtx_decode_layer_args, dst),'
+                   ' offsetof(vtx_decode_layer_args, early)); return 0;}\n')
+    exe = tmp_path / "probe_dl"
+    subprocess.run(["gcc", "-I", os.path.join(ROOT, "include"), str(src), "-o", str(exe)], check=True)
+    vals = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True).stdout.split()]
+    A = vtx_attn.DecodeLayerArgs
+    assert vals == [ctypes.sizeof(A), A.q.offset, A.positions.offset, A.k_cache_ptrs.offset, A.dst.offset,
+                    A.early.offset]
+
+
+def test_decode_layer_validation_without_device(lib):
+    """Unsupported operands are rejected before any device work; the
+    workspace query is host-only."""
+    import vtx_attn
+    a = vtx_attn.DecodeLayerArgs()
+    a.n_seq, a.n_head_q, a.n_head_kv, a.head_dim, a.kv_type = 1, 32, 8, 128, vtx_attn.F32
+    a.max_kv_len, a.freq_base, a.scale = 100, 1e6, 128 ** -0.5
+    assert lib.vtx_decode_layer(ctypes.byref(a), None, 0, None) == -2          # F32 cache: the two-call path
+    assert lib.vtx_decode_layer_workspace(ctypes.byref(a)) == ctypes.c_size_t(-1).value
+    a.kv_type, a.head_dim = vtx_attn.Q8_0, 64
+    assert lib.vtx_decode_layer(ctypes.byref(a), None, 0, None) == -5
+    a.head_dim, a.n_head_kv, a.n_head_q = 128, 3, 12
+    assert lib.vtx_decode_layer(ctypes.byref(a), None, 0, None) == -5          # Q8_0 needs an even head count
+    a.n_head_kv, a.n_head_q = 2, 32
+    assert lib.vtx_decode_layer(ctypes.byref(a), None, 0, None) == -5          # group of 16 > 8
+    assert lib.vtx_decode_layer(None, None, 0, None) == -1
+    a.n_head_kv, a.max_kv_len = 8, 7300
+    n = lib.vtx_decode_layer_workspace(ctypes.byref(a))
+    assert 0 < n < (1 << 24)

@@ -12,14 +12,16 @@ from vtx_cases import assert_close
 pytestmark = pytest.mark.gpu
 
 
+@pytest.mark.parametrize("fused", [True, False], ids=["fused", "two-calls"])
 @pytest.mark.parametrize("kv_type", [O.F16, O.Q8_0])
-def test_graph_decode_steps_match_oracle(kv_type):
+def test_graph_decode_steps_match_oracle(kv_type, fused):
     import torch
     from decode_step import DecodeStepGraph
     L, S, Hq, Hkv, D, W, steps = 2, 3, 8, 2, 128, 64, 30
     start = [5, 60, 70]                     # the last stream's ring has already wrapped
     rng = np.random.default_rng(50 + kv_type)
-    g = DecodeStepGraph(L, S, Hq, Hkv, D, kv_type, W, start)
+    g = DecodeStepGraph(L, S, Hq, Hkv, D, kv_type, W, start, fused=fused)
+    assert g.fused == fused
     hb = O.cache_head_bytes(kv_type, D)
     host_k = np.zeros((L, S, W, Hkv * hb), np.uint8)
     host_v = np.zeros_like(host_k)

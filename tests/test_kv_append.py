@@ -9,7 +9,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from vtx_cases import assert_close
+from vtx_cases import assert_close, f16_ulp_close as _f16_ulp_close, q8_close as _q8_close
 
 BASE = 1e6           # voxtral's dec_rope_theta (include/voxtral.h:41)
 
@@ -113,24 +113,6 @@ def _gpu_append(q, k, v, pos, slots, kv_type, rows, **kw):
                             kc, vc, kv_type, BASE, q=None if q is None else torch.from_numpy(q).to(dev), **kw)
     torch.cuda.synchronize()
     return (None if qo is None else qo.cpu().numpy()), kc.cpu().numpy(), vc.cpu().numpy()
-
-
-def _f16_ulp_close(got: np.ndarray, ref: np.ndarray) -> None:
-    g, r = got.astype(np.float32), ref.astype(np.float32)
-    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
-    assert np.all(np.abs(g - r) <= ulp), np.abs(g - r).max()
-
-
-def _q8_close(got: np.ndarray, ref: np.ndarray) -> None:
-    """Q8_0 rows: scales within one f16 ulp, values within one step (a float
-    that lands on a rounding boundary may differ in its last bit)."""
-    g = got.reshape(-1, 34)
-    r = ref.reshape(-1, 34)
-    gd, rd = g[:, :2].copy().view(np.float16).ravel(), r[:, :2].copy().view(np.float16).ravel()
-    _f16_ulp_close(gd, rd)
-    gq, rq = g[:, 2:].view(np.int8).astype(int), r[:, 2:].view(np.int8).astype(int)
-    assert np.abs(gq - rq).max() <= 1
-    assert (gq != rq).mean() < 0.01
 
 
 @pytest.mark.gpu

@@ -120,3 +120,23 @@ def assert_parity(got: np.ndarray, ggml: np.ndarray, fp64: np.ndarray, what: str
     v = O.parity_verdict(got, ggml, fp64)
     assert v["ok"], f"{what}: {v}"
     return v
+
+
+def f16_ulp_close(got: np.ndarray, ref: np.ndarray) -> None:
+    """Rotated K rows in half: within one f16 ulp (the device takes cos/sin in
+    double rounded to float, ggml's CPU cosf/sinf may differ in the last bit)."""
+    g, r = got.astype(np.float32), ref.astype(np.float32)
+    ulp = np.spacing(np.abs(ref).astype(np.float16)).astype(np.float32)
+    assert np.all(np.abs(g - r) <= ulp), np.abs(g - r).max()
+
+
+def q8_close(got: np.ndarray, ref: np.ndarray) -> None:
+    """Q8_0 rows: scales within one f16 ulp, values within one step (a float
+    that lands on a rounding boundary may differ in its last bit)."""
+    g = got.reshape(-1, 34)
+    r = ref.reshape(-1, 34)
+    gd, rd = g[:, :2].copy().view(np.float16).ravel(), r[:, :2].copy().view(np.float16).ravel()
+    f16_ulp_close(gd, rd)
+    gq, rq = g[:, 2:].view(np.int8).astype(int), r[:, 2:].view(np.int8).astype(int)
+    assert np.abs(gq - rq).max() <= 1
+    assert (gq != rq).mean() < 0.01

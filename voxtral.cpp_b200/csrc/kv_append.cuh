@@ -30,6 +30,48 @@
 
 namespace vtx {
 
+// ggml mode-0 rotation of one adjacent pair by (cos, sin) = c.  Shared by
+// every kernel that rotates Q or K, so all of them produce the same floats.
+__device__ __forceinline__ void rope_pair(float &x0, float &x1, float2 c) {
+    const float a0 = x0, a1 = x1;
+    x0 = a0 * c.x - a1 * c.y;
+    x1 = a0 * c.y + a1 * c.x;
+}
+
+// (cos, sin) of rotation pair i at position pos, as ggml's CPU rope cache:
+// theta_0 = (float)pos, theta_{i+1} = theta_i * theta_scale, then sin and cos
+// in double rounded to float.
+__device__ __forceinline__ float2 rope_cs(float theta) {
+    double sd, cd;
+    sincos((double)theta, &sd, &cd);
+    return make_float2((float)cd, (float)sd);
+}
+
+// One lane's E consecutive values of a head row written as Q8_0 into the
+// head's cache bytes `row` (blocks of 34 bytes: f16 d, then 32 int8): 32 / E
+// lanes share a block, amax by shuffles, d = amax/127 rounded to half,
+// q = round-half-even(x * 127/amax) -- ggml's CPU from_float.  Warp-collective.
+template <int E>
+__device__ __forceinline__ void store_q8_lane(const float (&x)[E], char *row, int lane) {
+    constexpr int LPB = 32 / E;
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
+#pragma unroll
+    for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    const float id = amax != 0.f ? 127.f / amax : 0.f;
+    char *blk = row + (lane / LPB) * 34;
+    if (lane % LPB == 0) *reinterpret_cast<__half *>(blk) = __float2half_rn(amax / 127.f);
+    // the block's values start 2 bytes in: 2-byte stores stay aligned
+    unsigned short *qs = reinterpret_cast<unsigned short *>(blk + 2 + (lane % LPB) * E);
+#pragma unroll
+    for (int i = 0; i < E; i += 2) {
+        const uint32_t q0 = (uint32_t)(__float2int_rn(x[i] * id) & 0xff);
+        const uint32_t q1 = (uint32_t)(__float2int_rn(x[i + 1] * id) & 0xff);
+        qs[i / 2] = (unsigned short)(q0 | (q1 << 8));
+    }
+}
+
 struct KvAppendArgs {
     int T, Hq, Hkv, kv_type;
     float theta_scale;
@@ -66,9 +108,7 @@ kv_append_kernel(const KvAppendArgs a)
     if (rope && threadIdx.x < D / 2) {
         float theta = (float)a.positions[t];
         for (int i = 0; i < (int)threadIdx.x; ++i) theta *= a.theta_scale;
-        double sd, cd;
-        sincos((double)theta, &sd, &cd);
-        cs[threadIdx.x] = make_float2((float)cd, (float)sd);
+        cs[threadIdx.x] = rope_cs(theta);
     }
     __syncthreads();
     const int slot = a.slots[t];
@@ -88,12 +128,7 @@ kv_append_kernel(const KvAppendArgs a)
         }
         if (kind != 2) {
 #pragma unroll
-            for (int j = 0; j < E / 2; ++j) {
-                const float2 c = cs[lane * E / 2 + j];
-                const float x0 = x[2 * j], x1 = x[2 * j + 1];
-                x[2 * j] = x0 * c.x - x1 * c.y;
-                x[2 * j + 1] = x0 * c.y + x1 * c.x;
-            }
+            for (int j = 0; j < E / 2; ++j) rope_pair(x[2 * j], x[2 * j + 1], cs[lane * E / 2 + j]);
         }
         if (kind == 0) {
             float *dst = a.q_out + (long long)t * a.qo_nb1 + (long long)h * D + lane * E;
@@ -114,23 +149,7 @@ kv_append_kernel(const KvAppendArgs a)
             for (int i = 0; i < E; i += 2)
                 *reinterpret_cast<__half2 *>(dst + i) = __floats2half2_rn(x[i], x[i + 1]);
         } else {                                            // Q8_0: 32 / E lanes per block
-            constexpr int LPB = 32 / E;
-            float amax = 0.f;
-#pragma unroll
-            for (int i = 0; i < E; ++i) amax = fmaxf(amax, fabsf(x[i]));
-#pragma unroll
-            for (int o = 1; o < LPB; o <<= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-            const float id = amax != 0.f ? 127.f / amax : 0.f;
-            char *blk = crow + (long long)h * (D / 32) * 34 + (lane / LPB) * 34;
-            if (lane % LPB == 0) *reinterpret_cast<__half *>(blk) = __float2half_rn(amax / 127.f);
-            // the block's values start 2 bytes in: 2-byte stores stay aligned
-            unsigned short *qs = reinterpret_cast<unsigned short *>(blk + 2 + (lane % LPB) * E);
-#pragma unroll
-            for (int i = 0; i < E; i += 2) {
-                const uint32_t q0 = (uint32_t)(__float2int_rn(x[i] * id) & 0xff);
-                const uint32_t q1 = (uint32_t)(__float2int_rn(x[i + 1] * id) & 0xff);
-                qs[i / 2] = (unsigned short)(q0 | (q1 << 8));
-            }
+            store_q8_lane<E>(x, crow + (long long)h * (D / 32) * 34, lane);
         }
     }
 }

@@ -34,6 +34,7 @@
 #include "kv_append.cuh"
 #include "enc_stitch.cuh"
 #include "out_proj.cuh"
+#include "decode_layer.cuh"
 
 using namespace vtx;
 
@@ -798,6 +799,61 @@ int decode_batched_impl(const vtx_decode_batch *b, void *scratch, size_t scratch
     return launch_split(a, D, b->kv_type, sp.maxr, grid, st);
 }
 
+// Fused decode layer (decode_layer.cuh): splits per (stream, KV head) so one
+// wave covers the GPU, at least one 16-key tile per warp; workspace = the
+// split partials (O, then (m, l)) and one arrival counter per (stream, KV
+// head), which must be zero before the first call (every call leaves it so).
+struct LayerPlan {
+    int n_splits = 1;
+    size_t o_bytes = 0, ml_bytes = 0, flag_bytes = 0, bytes = 0;
+};
+
+int check_layer_args(const vtx_decode_layer_args *p) {
+    if (!p) return VTX_ERR_NULL;
+    if (p->n_seq < 0 || p->n_head_q <= 0 || p->n_head_kv <= 0 || p->n_head_q % p->n_head_kv || p->max_kv_len < 0)
+        return VTX_ERR_SHAPE;
+    if (p->head_dim != 128 || p->n_head_q / p->n_head_kv > 8) return VTX_ERR_UNSUPPORTED;
+    if (p->kv_type != VTX_TYPE_F16 && p->kv_type != VTX_TYPE_Q8_0) return VTX_ERR_TYPE;
+    if (p->kv_type == VTX_TYPE_Q8_0 && p->n_head_kv % 2) return VTX_ERR_UNSUPPORTED;
+    if (!(p->freq_base > 0.0f)) return VTX_ERR_SHAPE;
+    if ((long long)p->n_seq * p->n_head_kv > (1LL << 24)) return VTX_ERR_UNSUPPORTED;
+    return VTX_OK;
+}
+
+LayerPlan plan_layer(const vtx_decode_layer_args *p, int sms) {
+    LayerPlan lp;
+    const long long items = (long long)p->n_seq * p->n_head_kv;
+    const int tiles = (std::max(1, p->max_kv_len) + 15) / 16;
+    const int minb = p->kv_type == VTX_TYPE_Q8_0 ? LayerCfg<8>::MINB : LayerCfg<1>::MINB;   // CTAs per SM
+    const long long by_wave = std::max<long long>(1, (long long)sms * minb / std::max<long long>(1, items));
+    const int w = p->kv_type == VTX_TYPE_Q8_0 ? LayerCfg<8>::W : LayerCfg<1>::W;           // warps per CTA
+    lp.n_splits = (int)std::max<long long>(1, std::min<long long>(by_wave, (tiles + w - 1) / w));
+    const int G = p->n_head_q / p->n_head_kv;
+    if (lp.n_splits > 1) {
+        const size_t rows = (size_t)items * lp.n_splits * G;
+        lp.o_bytes = align_up(rows * p->head_dim * 4, 256);
+        lp.ml_bytes = align_up(rows * 8, 256);
+        lp.flag_bytes = align_up((size_t)items * 4, 256);
+    }
+    lp.bytes = lp.o_bytes + lp.ml_bytes + lp.flag_bytes;
+    return lp;
+}
+
+template <int KVT>
+int launch_decode_layer_t(const DecodeLayerArgs &a, unsigned ctas, cudaStream_t st) {
+    using C = LayerCfg<KVT>;
+    static std::atomic<int> attr_done[kMaxDevices];
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_done[dev].load(std::memory_order_acquire)) {
+        if (cudaFuncSetAttribute(fa_decode_layer_kernel<KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+            cudaSuccess)
+            return VTX_ERR_CUDA;
+        attr_done[dev].store(1, std::memory_order_release);
+    }
+    return launch_pdl(fa_decode_layer_kernel<KVT>, dim3(ctas), dim3(C::NT), C::SMEM, st, a);
+}
+
 }  // namespace
 
 // ================================================================================
@@ -1053,6 +1109,57 @@ int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_len, int3
     if (rc != VTX_OK) return rc;
     return launch_pdl(decode_advance_kernel, dim3((unsigned)((n + 255) / 256)), dim3(256), 0,
                       static_cast<cudaStream_t>(stream), positions, slots, kv_len, (int)n, (int)window);
+}
+
+size_t vtx_decode_layer_workspace(const vtx_decode_layer_args *p) {
+    if (check_layer_args(p) != VTX_OK) return (size_t)-1;
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaGetLastError();
+    return plan_layer(p, sms).bytes;
+}
+
+int vtx_decode_layer(const vtx_decode_layer_args *p, void *workspace, size_t workspace_bytes, void *stream) {
+    int rc = check_layer_args(p);
+    if (rc != VTX_OK) return rc;
+    if (p->n_seq == 0) return VTX_OK;
+    if (!p->q || !p->k || !p->v || !p->dst || !p->positions || !p->slots || !p->kv_len || !p->k_cache_ptrs ||
+        !p->v_cache_ptrs)
+        return VTX_ERR_NULL;
+    const uintptr_t al = reinterpret_cast<uintptr_t>(p->q) | reinterpret_cast<uintptr_t>(p->k) |
+                         reinterpret_cast<uintptr_t>(p->v) | reinterpret_cast<uintptr_t>(p->dst) | p->q_nb1 |
+                         p->k_nb1 | p->v_nb1 | p->dst_nb1 | p->cache_nb1;
+    if (al % 16) return VTX_ERR_STRIDE;
+    const size_t hb = p->kv_type == VTX_TYPE_Q8_0 ? (size_t)p->head_dim / 32 * 34 : (size_t)p->head_dim * 2;
+    if (p->cache_nb1 < hb * p->n_head_kv) return VTX_ERR_STRIDE;
+    DeviceState *ds = nullptr;
+    rc = ensure_device(&ds);
+    if (rc != VTX_OK) return rc;
+    const LayerPlan lp = plan_layer(p, ds->sms);
+    if (workspace_bytes < lp.bytes) return VTX_ERR_WORKSPACE;
+    if (lp.bytes && (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256)) return VTX_ERR_WORKSPACE;
+    DecodeLayerArgs a{};
+    a.n_seq = p->n_seq; a.Hq = p->n_head_q; a.Hkv = p->n_head_kv; a.G = p->n_head_q / p->n_head_kv;
+    a.q = p->q; a.k = p->k; a.v = p->v;
+    a.q_nb1 = (long long)(p->q_nb1 / 4); a.k_nb1 = (long long)(p->k_nb1 / 4); a.v_nb1 = (long long)(p->v_nb1 / 4);
+    a.positions = p->positions; a.slots = p->slots; a.kv_len = p->kv_len;
+    a.k_ptrs = p->k_cache_ptrs; a.v_ptrs = p->v_cache_ptrs;
+    a.cache_nb1 = (long long)p->cache_nb1;
+    a.theta_scale = std::pow(p->freq_base, -2.0f / (float)p->head_dim);   // as ggml: powf on the host
+    a.cx = p->scale * kLog2e;
+    a.dst = p->dst; a.dst_nb1 = (long long)(p->dst_nb1 / 4);
+    a.n_splits = lp.n_splits;
+    char *ws = static_cast<char *>(workspace);
+    if (lp.bytes) {
+        a.part_o = reinterpret_cast<float *>(ws);
+        a.part_ml = reinterpret_cast<float *>(ws + lp.o_bytes);
+        a.flags = reinterpret_cast<unsigned *>(ws + lp.o_bytes + lp.ml_bytes);
+    }
+    a.early = p->early ? 1 : 0;
+    a.err = ds->err;
+    const unsigned ctas = (unsigned)((long long)p->n_seq * p->n_head_kv * lp.n_splits);
+    cudaStream_t st = static_cast<cudaStream_t>(stream);
+    return p->kv_type == VTX_TYPE_F16 ? launch_decode_layer_t<1>(a, ctas, st) : launch_decode_layer_t<8>(a, ctas, st);
 }
 
 int vtx_encoder_chunk_plan(int32_t total_mel_frames, vtx_enc_chunk *chunks, int32_t max_chunks,

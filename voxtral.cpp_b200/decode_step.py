@@ -6,8 +6,10 @@ scheduling :1921-1973, :2086-2101) and keeps the cache window with a host-side
 shift-left memmove (:1237-1266, :2444-2447).  This helper captures one step of
 the attention path for all layers once, as a CUDA graph:
 
-    for each layer:  vtx_kv_append          (RoPE of Q/K, K/V into the ring row)
-                     vtx_flash_attn_decode_batched   (attention over the ring)
+    for each layer:  vtx_decode_layer       (RoPE of Q/K, K/V into the ring row,
+                                             attention over the ring, one launch)
+                     -- or, with fused=False (and for F32 caches), the two calls
+                     vtx_kv_append + vtx_flash_attn_decode_batched
     then:            vtx_decode_advance     (positions, ring slots, lengths + 1)
 
 and replays it per token with no host work: positions, ring slots and key
@@ -27,10 +29,12 @@ import vtx_attn
 
 class DecodeStepGraph:
     def __init__(self, n_layers: int, n_seq: int, n_head_q: int, n_head_kv: int, head_dim: int, kv_type: int,
-                 window: int, start_len, rope_base: float = 1e6, device: Optional[torch.device] = None):
+                 window: int, start_len, rope_base: float = 1e6, device: Optional[torch.device] = None,
+                 fused: bool = True):
         """start_len: tokens already in each stream's cache (its prefill), one
         int per stream; the next token goes to ring slot start_len % window at
-        position start_len."""
+        position start_len.  fused: one vtx_decode_layer launch per layer
+        (F16 / Q8_0 caches, head_dim 128) instead of append + attention."""
         dev = device or torch.device("cuda", torch.cuda.current_device())
         self.dev, self.L, self.S, self.Hq, self.Hkv, self.D = dev, n_layers, n_seq, n_head_q, n_head_kv, head_dim
         self.kv_type, self.W, self.base = kv_type, window, rope_base
@@ -54,8 +58,18 @@ class DecodeStepGraph:
         self.v = torch.zeros_like(self.k)
         self.q_rot = torch.zeros_like(self.q)
         self.out = torch.zeros_like(self.q)
+        self.fused = fused and kv_type in (vtx_attn.F16, vtx_attn.Q8_0) and head_dim == 128
         self.plans: List[vtx_attn.DecodeBatchPlan] = []
-        for l in range(n_layers):
+        self.layer_plans: List[vtx_attn.DecodeLayerPlan] = []
+        for l in range(n_layers if self.fused else 0):
+            # layer 0 follows vtx_decode_advance, which moves the counters: it
+            # waits before reading anything; later layers may stream their ring
+            # while the previous layer's kernel still runs
+            self.layer_plans.append(vtx_attn.DecodeLayerPlan(
+                [self.k_cache[l, s] for s in range(n_seq)], [self.v_cache[l, s] for s in range(n_seq)],
+                self.positions, self.slots, self.kv_len, n_head_q, n_head_kv, head_dim, kv_type, self.row, window,
+                head_dim ** -0.5, rope_base, early=l > 0))
+        for l in range(0 if self.fused else n_layers):
             p = vtx_attn.DecodeBatchPlan([self.k_cache[l, s] for s in range(n_seq)],
                                          [self.v_cache[l, s] for s in range(n_seq)], self.kv_len, n_head_q,
                                          n_head_kv, head_dim, kv_type, self.row, hb, window, head_dim ** -0.5,
@@ -75,7 +89,9 @@ class DecodeStepGraph:
                            self.kv_type, self.base, cache_nb1=self.row)
 
     def _step_calls(self) -> None:
-        for l in range(self.L):
+        for l, lp in enumerate(self.layer_plans):
+            lp(self.q[l], self.k[l], self.v[l], self.out[l], self.stream)
+        for l in range(0 if self.fused else self.L):
             vtx_attn.kv_append(self.k[l], self.v[l], self.positions, self.slots, None, None, self.kv_type, self.base,
                                q=self.q[l], q_out=self.q_rot[l], k_cache_ptrs=self.k_ptrs[l],
                                v_cache_ptrs=self.v_ptrs[l], cache_nb1=self.row, stream=self.stream)
@@ -134,10 +150,11 @@ def _main() -> None:
     ap.add_argument("--keys", type=int, default=7300, help="tokens already in the ring")
     ap.add_argument("--kv", default="q8_0", choices=["q8_0", "f16"])
     ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--unfused", action="store_true", help="append + attention as two calls per layer")
     args = ap.parse_args()
     kvt = vtx_attn.Q8_0 if args.kv == "q8_0" else vtx_attn.F16
     L, start = args.layers, args.keys
-    g = DecodeStepGraph(L, 1, 32, 8, 128, kvt, 8192, [start], 1e6)
+    g = DecodeStepGraph(L, 1, 32, 8, 128, kvt, 8192, [start], 1e6, fused=not args.unfused)
     gen = torch.Generator(device=g.dev)
     gen.manual_seed(1)
     for l in range(L):

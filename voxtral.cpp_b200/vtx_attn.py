@@ -71,6 +71,21 @@ class KvAppendArgs(ctypes.Structure):
                 ("cache_nb1", ctypes.c_size_t), ("reserved", ctypes.c_int32 * 4)]
 
 
+class DecodeLayerArgs(ctypes.Structure):
+    """vtx_decode_layer_args (include/vtx_fa.h)."""
+    _fields_ = [("n_seq", ctypes.c_int32), ("n_head_q", ctypes.c_int32),
+                ("n_head_kv", ctypes.c_int32), ("head_dim", ctypes.c_int32),
+                ("kv_type", ctypes.c_int32), ("max_kv_len", ctypes.c_int32),
+                ("freq_base", ctypes.c_float), ("scale", ctypes.c_float),
+                ("q", ctypes.c_void_p), ("q_nb1", ctypes.c_size_t),
+                ("k", ctypes.c_void_p), ("k_nb1", ctypes.c_size_t),
+                ("v", ctypes.c_void_p), ("v_nb1", ctypes.c_size_t),
+                ("positions", ctypes.c_void_p), ("slots", ctypes.c_void_p), ("kv_len", ctypes.c_void_p),
+                ("k_cache_ptrs", ctypes.c_void_p), ("v_cache_ptrs", ctypes.c_void_p),
+                ("cache_nb1", ctypes.c_size_t), ("dst", ctypes.c_void_p), ("dst_nb1", ctypes.c_size_t),
+                ("early", ctypes.c_int32), ("reserved", ctypes.c_int32 * 3)]
+
+
 class OutProjArgs(ctypes.Structure):
     """vtx_out_proj_args (include/vtx_fa.h)."""
     _fields_ = [("attn", ctypes.c_void_p), ("head_block", ctypes.c_int32), ("reserved", ctypes.c_int32),
@@ -131,6 +146,10 @@ def load(path: str = LIB_PATH):
     L.vtx_encoder_stitch.restype = ctypes.c_int
     L.vtx_attn_out_proj.argtypes = [P(OutProjArgs), ctypes.c_void_p]
     L.vtx_attn_out_proj.restype = ctypes.c_int
+    L.vtx_decode_layer.argtypes = [P(DecodeLayerArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]
+    L.vtx_decode_layer.restype = ctypes.c_int
+    L.vtx_decode_layer_workspace.argtypes = [P(DecodeLayerArgs)]
+    L.vtx_decode_layer_workspace.restype = ctypes.c_size_t
     _lib = L
     return L
 
@@ -310,6 +329,55 @@ def kv_append(k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor, slots: 
     s = stream if stream is not None else torch.cuda.current_stream(k.device)
     _check(load().vtx_kv_append(ctypes.byref(a), ctypes.c_void_p(s.cuda_stream)), "vtx_kv_append")
     return q_out
+
+
+class DecodeLayerPlan:
+    """vtx_decode_layer over a fixed set of per-stream caches: RoPE of Q and K,
+    the new K/V row into ring slot ``slots[s]`` and decode attention over rows
+    [0, kv_len[s]), one launch per call.  The counters (positions, slots,
+    kv_len) and the cache pointer arrays live on the device, so a call can be
+    captured in a CUDA graph and replayed while the counters advance."""
+
+    def __init__(self, k_bufs: Sequence[torch.Tensor], v_bufs: Sequence[torch.Tensor], positions: torch.Tensor,
+                 slots: torch.Tensor, kv_len: torch.Tensor, n_head_q: int, n_head_kv: int, head_dim: int,
+                 kv_type: int, cache_nb1: int, max_kv_len: int, scale: float, freq_base: float = 1e6,
+                 early: bool = False):
+        dev = kv_len.device
+        self.k_ptrs = torch.tensor([t.data_ptr() for t in k_bufs], dtype=torch.int64, device=dev)
+        self.v_ptrs = torch.tensor([t.data_ptr() for t in v_bufs], dtype=torch.int64, device=dev)
+        self.keep = (list(k_bufs), list(v_bufs), positions, slots, kv_len)
+        a = DecodeLayerArgs()
+        a.n_seq, a.n_head_q, a.n_head_kv, a.head_dim = len(k_bufs), n_head_q, n_head_kv, head_dim
+        a.kv_type, a.max_kv_len, a.freq_base, a.scale = kv_type, max_kv_len, freq_base, scale
+        a.positions, a.slots, a.kv_len = positions.data_ptr(), slots.data_ptr(), kv_len.data_ptr()
+        a.k_cache_ptrs, a.v_cache_ptrs, a.cache_nb1 = self.k_ptrs.data_ptr(), self.v_ptrs.data_ptr(), cache_nb1
+        a.early = 1 if early else 0
+        self.args = a
+        need = load().vtx_decode_layer_workspace(ctypes.byref(a))
+        if need == ctypes.c_size_t(-1).value:
+            raise VtxError(-3, "decode layer rejected")
+        self.need = int(need)
+        # zeroed once: the split-arrival counters start at 0 and every call leaves them there
+        self.workspace = torch.zeros(max(self.need, 1), dtype=torch.uint8, device=dev)
+
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: Optional[torch.Tensor] = None,
+                 stream: Optional[torch.cuda.Stream] = None) -> torch.Tensor:
+        """q: (n_seq, Hq, D), k/v: (n_seq, Hkv, D) float32, heads contiguous;
+        returns (n_seq, Hq, D) float32."""
+        for t in (q, k, v):
+            if t.dtype != torch.float32 or t.stride(2) != 1 or t.stride(1) != t.shape[2]:
+                raise VtxError(-4, "q/k/v must be float32 with heads contiguous")
+        if out is None:
+            out = torch.empty_like(q)
+        a = self.args
+        a.q, a.q_nb1 = q.data_ptr(), q.stride(0) * 4
+        a.k, a.k_nb1 = k.data_ptr(), k.stride(0) * 4
+        a.v, a.v_nb1 = v.data_ptr(), v.stride(0) * 4
+        a.dst, a.dst_nb1 = out.data_ptr(), out.stride(0) * 4
+        s = stream if stream is not None else torch.cuda.current_stream(q.device)
+        _check(load().vtx_decode_layer(ctypes.byref(a), self.workspace.data_ptr(), self.workspace.numel(),
+                                       ctypes.c_void_p(s.cuda_stream)), "vtx_decode_layer")
+        return out
 
 
 # ---- realtime encoder: chunk plan and device-side stitch ---------------------
