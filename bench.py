@@ -296,8 +296,31 @@ def run_encoder_e2e(args, dev, world, rank):
     dt = barrier_max(time.perf_counter() - t0, world)
     h2d = host_in[0].numel() * host_in.element_size() * L
     d2h = host_out[0].numel() * host_out.element_size() * L
-    return {"value": round(enc_flops_per_layer() * L * steps * world / dt / 1e12, 3), "unit": "TFLOP/s",
+    # The host link alone: one clip's inputs H2D and its outputs D2H, each
+    # direction timed by itself on its stream (CUDA events).  With the three
+    # streams overlapped the step cannot beat the slower direction.
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def link_s(copy, stream):
+        with torch.cuda.stream(stream):
+            e0.record(stream)
+            for l in range(L):
+                copy(l)
+            e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) * 1e-3
+
+    t_h2d = link_s(lambda l: dbuf[l % nbuf].copy_(host_in[l], non_blocking=True), s_h2d)
+    t_d2h = link_s(lambda l: host_out[l].copy_(dout[l % nbuf], non_blocking=True), s_d2h)
+    bound_s = max(t_h2d, t_d2h)
+    value = enc_flops_per_layer() * L * steps * world / dt / 1e12
+    bound_tflops = enc_flops_per_layer() * L * world / bound_s / 1e12
+    return {"value": round(value, 3), "unit": "TFLOP/s",
             "h2d_bytes_per_step": int(h2d), "d2h_bytes_per_step": int(d2h), "steps": steps,
+            "host_link": {"h2d_GBps": round(h2d / t_h2d / 1e9, 1), "d2h_GBps": round(d2h / t_d2h / 1e9, 1),
+                          "bound_tflops": round(bound_tflops, 3), "frac_of_bound": round(value / bound_tflops, 3),
+                          "how": "one clip's pinned copies per direction alone (CUDA events); the bound is the "
+                                 "slower direction, since the three streams overlap"},
             "how": "pinned host Q/K/V per layer -> H2D stream, vtx_flash_attn_ext on compute stream, "
                    "D2H stream; host wall clock after synchronize, max over ranks"}
 

@@ -159,15 +159,18 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             if (!ok) break;
             const char *src = a32(s);
             char *dst = a16(s);
-            const int c8 = t & 7;
-#pragma unroll
-            for (int it = 0; it < C::BM / 16; ++it) {
-                const int row = it * 16 + (t >> 3);
-                const float4 x0 = *reinterpret_cast<const float4 *>(src + row * 256 + c8 * 32);
-                const float4 x1 = *reinterpret_cast<const float4 *>(src + row * 256 + c8 * 32 + 16);
-                *reinterpret_cast<uint4 *>(dst + row * 128 + ((c8 ^ (row & 7)) << 4)) =
-                    make_uint4(pack_half2(x0.x, x0.y), pack_half2(x0.z, x0.w), pack_half2(x1.x, x1.y),
-                               pack_half2(x1.z, x1.w));
+            // warp q converts rows 32q .. 32q + 31, two rows (512 contiguous
+            // bytes, conflict-free) per instruction: lane l takes floats
+            // 4 (l % 16) .. + 3 of row 2 it + l / 16 and writes their halves
+            // as one 8-byte half of a swizzled 16-byte chunk (a half-warp
+            // writes one whole 128-byte row: conflict-free as well)
+            const int q = t >> 5, f4 = lane & 15;
+#pragma unroll 4
+            for (int it = 0; it < 16; ++it) {
+                const int row = 32 * q + 2 * it + (lane >> 4);
+                const float4 x = *reinterpret_cast<const float4 *>(src + row * 256 + f4 * 16);
+                *reinterpret_cast<uint2 *>(dst + row * 128 + (((f4 >> 1) ^ (row & 7)) << 4) + (f4 & 1) * 8) =
+                    make_uint2(pack_half2(x.x, x.y), pack_half2(x.z, x.w));
             }
             fence_proxy_async_smem();
             __syncwarp();
