@@ -257,10 +257,10 @@ VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_l
  * - dst: [n_seq] rows of n_head_q * head_dim F32 (ggml's result for n_q = 1).
  * - head_dim 128, n_head_q / n_head_kv <= 8; Q8_0 needs an even n_head_kv.
  *   q, k, v, dst, the cache bases and every stride 16-byte aligned.
- * - early = 1: the cache rows other than slots[s], kv_len, slots and the
- *   pointer arrays may be read while the kernel launched just before still
- *   runs (they must be complete before it); only q, k, v and positions are
- *   waited for.  early = 0 reads nothing before that kernel completes.
+ * - early = 1: the cache rows other than slots[s], positions, kv_len, slots
+ *   and the pointer arrays may be read while the kernel launched just before
+ *   still runs (they must be complete before it); only q, k and v are waited
+ *   for.  early = 0 reads nothing before that kernel completes.
  * - workspace: vtx_decode_layer_workspace(args) bytes, 256-byte aligned:
  *   split partials and one arrival counter per stream and KV head.  Zero it
  *   once before the first call (cudaMemset); every completed call leaves it

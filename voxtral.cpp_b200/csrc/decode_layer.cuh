@@ -56,7 +56,7 @@ struct DecodeLayerArgs {
     int n_splits;                              // key splits per (stream, head) in the grid (the most used)
     float *part_o, *part_ml;                   // split partials (n_splits > 1)
     unsigned *flags;                           // one arrival counter per (stream, KV head), zero between calls
-    int early;                                 // ring rows may be read before the dependency wait
+    int early;                                 // ring rows and counters may be read before the dependency wait
     int *err;
 };
 
@@ -135,7 +135,7 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
     const int kv_raw = a.kv_len[b];
     const int fresh = a.slots[b];
     const void *kp0 = a.k_ptrs[b], *vp0 = a.v_ptrs[b];
-    const int pos_pre = !a.early && threadIdx.x < 64 ? a.positions[b] : 0;   // early: read after the wait
+    const int pos = threadIdx.x < 64 ? a.positions[b] : 0;    // the RoPE position (table threads)
     // this stream's splits, from its key count: at most n_splits, at least one
     // 16-key tile per warp each (so short caches use fewer CTAs and merges)
     const int kv_len = max(0, kv_raw);
@@ -229,13 +229,19 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
 #pragma unroll
     for (int i = 0; i < C::STAGES; ++i) issue(i);
 
+    // ---- the CTA's (cos, sin) table: thread i < 64 runs the float angle
+    //      recurrence i steps (ggml's rope cache), then one sincos (with early
+    //      = 1 the positions, like the ring, come before the dependency wait)
+    if (threadIdx.x < 64) {
+        float th = (float)pos;
+        for (int i = 0; i < (int)threadIdx.x; ++i) th *= a.theta_scale;
+        reinterpret_cast<float2 *>(smem + C::CS_OFF)[threadIdx.x] = rope_cs(th);
+    }
+
     // ---- dependency wait; Q of the group into registers (warps with tiles) ----
     if (a.early) grid_dep_wait();
     const float *qg = a.q + (long long)b * a.q_nb1 + (long long)g * a.G * D;
     constexpr int NB = D / 8, NJ = D / 16, KC = D / 16, NBLK = D / 32;
-    // F16: lane holds row l/4 (the query head), columns 2(l%4)+{0,1} (+8) of
-    // every 16-column chunk.  Q8_0: lane (r, c) holds head r's values 32j + 4c..
-    // and 32j + 16 + 4c.. of every block j.
     // F16: every warp with tiles loads its A fragments (row l/4 = the query
     // head, columns 2(l%4)+{0,1} and +8 of every 16-column chunk).  Q8_0: warp
     // j < 4 loads block j (lane (r, c): head r's values 32j + 4c.. and
@@ -260,14 +266,7 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
             }
         }
     }
-    // ---- the CTA's (cos, sin) table: thread i < 64 runs the float angle
-    //      recurrence i steps (ggml's rope cache), then one sincos
-    if (threadIdx.x < 64) {
-        float th = (float)(a.early ? a.positions[b] : pos_pre);
-        for (int i = 0; i < (int)threadIdx.x; ++i) th *= a.theta_scale;
-        reinterpret_cast<float2 *>(smem + C::CS_OFF)[threadIdx.x] = rope_cs(th);
-    }
-    __syncthreads();
+    __syncthreads();                                           // the table is complete
     table_ready = true;
     if (f_local >= 0 && f_local < C::STAGES) {                 // the new row's tile was issued above
         const int k0 = kb + (warp + W * f_local) * KEYS;
@@ -384,8 +383,11 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
         l += __shfl_xor_sync(0xffffffffu, l, 2);
         if (qrow < a.G) {
             float *so = st_o + (warp * C::GMAX + qrow) * C::SP;
+            if (my_tiles > 0) {                                // an empty warp's O is never read
 #pragma unroll
-            for (int nb = 0; nb < NB; ++nb) *reinterpret_cast<float2 *>(so + nb * 8 + kk) = make_float2(o[nb][0], o[nb][1]);
+                for (int nb = 0; nb < NB; ++nb)
+                    *reinterpret_cast<float2 *>(so + nb * 8 + kk) = make_float2(o[nb][0], o[nb][1]);
+            }
             if ((lane & 3) == 0) st_ml[warp * C::GMAX + qrow] = make_float2(m_run[0], l);
         }
     } else {
@@ -399,10 +401,12 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
             const int hh = 2 * (lane & 3) + h;
             if (hh < a.G) {
                 float *so = st_o + (warp * C::GMAX + hh) * C::SP;
+                if (my_tiles > 0) {                            // an empty warp's O is never read
 #pragma unroll
-                for (int j = 0; j < NJ; ++j) {
-                    so[16 * j + d0] = o[j][h];
-                    so[16 * j + d0 + 8] = o[j][2 + h];
+                    for (int j = 0; j < NJ; ++j) {
+                        so[16 * j + d0] = o[j][h];
+                        so[16 * j + d0 + 8] = o[j][2 + h];
+                    }
                 }
                 if (d0 == 0) st_ml[warp * C::GMAX + hh] = make_float2(m_run[h], l);
             }
@@ -411,34 +415,40 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
     __syncthreads();
 
     // ---- merge the warps (fixed order); final row or this split's partial ----
-    // the factors 2^(m_w - M) and the row sums once per (warp, row)
+    // the factors 2^(m_w - M) and the row sums once per (warp, row): thread
+    // r * W + w takes (row r, warp w); the row's max and sum by shuffles over
+    // its W lanes (W divides 32)
     const long long work = ((long long)b * a.Hkv + g) * a.n_splits + sp;
     float *st_f = reinterpret_cast<float *>(smem + C::ST_F);
-    if (threadIdx.x < a.G) {
-        const int r = threadIdx.x;
-        float M = -INFINITY;
+    static_assert(W <= 32 && (W & (W - 1)) == 0 && C::GMAX * W % 32 == 0 && C::GMAX * W <= C::NT,
+                  "a row's W lanes inside one warp, whole warps");
+    if (threadIdx.x < C::GMAX * W) {
+        const int r = threadIdx.x / W, w = threadIdx.x % W;
+        const float2 ml = r < a.G ? st_ml[w * C::GMAX + r] : make_float2(-INFINITY, 0.f);
+        float M = ml.y > 0.f ? ml.x : -INFINITY;
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-            const float2 ml = st_ml[w * C::GMAX + r];
-            if (ml.y > 0.f) M = fmaxf(M, ml.x);
-        }
-        float L = 0.f;
+        for (int x = W / 2; x > 0; x >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, x));
+        const float f = ml.y > 0.f ? ex2(ml.x - M) : 0.f;
+        float L = f * ml.y;
 #pragma unroll
-        for (int w = 0; w < W; ++w) {
-            const float2 ml = st_ml[w * C::GMAX + r];
-            const float f = ml.y > 0.f ? ex2(ml.x - M) : 0.f;
+        for (int x = W / 2; x > 0; x >>= 1) L += __shfl_xor_sync(0xffffffffu, L, x);
+        if (r < a.G) {
             st_f[w * C::GMAX + r] = f;
-            L = fmaf(f, ml.y, L);
+            if (w == 0) {
+                st_f[W * C::GMAX + r] = nsp == 1 ? (L == 0.f ? 0.f : 1.f / L) : L;
+                if (nsp > 1) reinterpret_cast<float2 *>(a.part_ml)[work * a.G + r] = make_float2(M, L);
+            }
         }
-        st_f[W * C::GMAX + r] = nsp == 1 ? (L == 0.f ? 0.f : 1.f / L) : L;
-        if (nsp > 1) reinterpret_cast<float2 *>(a.part_ml)[work * a.G + r] = make_float2(M, L);
     }
     __syncthreads();
     for (int it = threadIdx.x; it < a.G * D; it += C::NT) {
         const int r = it / D, d = it % D;
         float O = 0.f;
 #pragma unroll
-        for (int w = 0; w < W; ++w) O = fmaf(st_f[w * C::GMAX + r], st_o[(w * C::GMAX + r) * C::SP + d], O);
+        for (int w = 0; w < W; ++w) {
+            const float f = st_f[w * C::GMAX + r];
+            if (f != 0.f) O = fmaf(f, st_o[(w * C::GMAX + r) * C::SP + d], O);   // empty warps wrote no O
+        }
         const float x = st_f[W * C::GMAX + r];
         if (nsp == 1) a.dst[(long long)b * a.dst_nb1 + (long long)(g * a.G + r) * D + d] = O * x;
         else a.part_o[(work * a.G + r) * D + d] = O;
