@@ -137,10 +137,12 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
     const void *kp0 = a.k_ptrs[b], *vp0 = a.v_ptrs[b];
     const int pos = threadIdx.x < 64 ? a.positions[b] : 0;    // the RoPE position (table threads)
     // this stream's splits, from its key count: at most n_splits, at least one
-    // 16-key tile per warp each (so short caches use fewer CTAs and merges)
+    // 16-key tile per warp each (so short caches use fewer CTAs and merges),
+    // and none up to two tiles per warp (measured: a Q8_0 cache of 500 keys
+    // 6.4 us in one CTA per head vs 7.6 us in two with the merge)
     const int kv_len = max(0, kv_raw);
     const int tiles_b = (kv_len + KEYS - 1) / KEYS;
-    const int s_eff = max(1, min(a.n_splits, (tiles_b + W - 1) / W));
+    const int s_eff = tiles_b <= 2 * W ? 1 : max(1, min(a.n_splits, (tiles_b + W - 1) / W));
     const int chunk = max(1, (tiles_b + s_eff - 1) / s_eff) * KEYS;
     const int nsp = max(1, (kv_len + chunk - 1) / chunk);
     const int kb = sp * chunk;
