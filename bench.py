@@ -918,9 +918,13 @@ def run_out_proj(args, rank, world, local):
     configs[1] encoder (1500 tokens, 20 x 64 -> 1280, + attn_o_bias +
     residual; 32 layers) and configs[2] decoder prefill (391 tokens, 32 x 128
     -> 3072, + residual; 30 layers), each layer with its own attention output,
-    weight and residual (more than L2 per step), graph-replayed.  Roofline:
-    bytes = A (F32) + W (f16) + residual + output, FLOPs = 2 M N K; the bound
-    is whichever of the two takes longer at the measured peaks."""
+    weight and residual (more than L2 per step), graph-replayed.  Two A
+    operands: the attention's F32 result (ggml's node output, converted to
+    f16 in the kernel) and its F16 result (vtx_flash_attn_ext with an F16
+    dst: the same rounding done once in the attention epilogue), key
+    "f16_attention".  Roofline: bytes = A + W (f16) + residual + output,
+    FLOPs = 2 M N K; the bound is whichever takes longer at the measured
+    peaks."""
     import torch
     import vtx_attn
 
@@ -932,55 +936,63 @@ def run_out_proj(args, rank, world, local):
         K = Hq * Dv
         g = torch.Generator(device=dev)
         g.manual_seed(900 + rank)
-        A = torch.randn((L, 1, M, Hq, Dv), generator=g, device=dev) * 0.3
+        A32 = torch.randn((L, 1, M, Hq, Dv), generator=g, device=dev) * 0.3
         W = (torch.randn((L, N, K), generator=g, device=dev) / K ** 0.5).half()
         R = torch.randn((L, M, N), generator=g, device=dev)
         Bv = torch.randn((L, N), generator=g, device=dev) if has_bias else None
         Y = torch.empty((L, M, N), device=dev)
         stream = torch.cuda.Stream(device=dev)
 
-        def step():
-            for l in range(L):
-                vtx_attn.out_proj(A[l], W[l], Bv[l] if has_bias else None, R[l], out=Y[l], stream=stream)
+        def measure(A):
+            def step():
+                for l in range(L):
+                    vtx_attn.out_proj(A[l], W[l], Bv[l] if has_bias else None, R[l], out=Y[l], stream=stream)
 
-        with torch.cuda.stream(stream):
-            step()
-        torch.cuda.synchronize()
-        graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(graph, stream=stream):
-            step()
-        for _ in range(3):
-            graph.replay()
-        torch.cuda.synchronize()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        reps = max(3, args.steps)
-        with torch.cuda.stream(stream):
-            e0.record(stream)
-            for _ in range(reps):
+            with torch.cuda.stream(stream):
+                step()
+            torch.cuda.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                step()
+            for _ in range(3):
                 graph.replay()
-            e1.record(stream)
-        torch.cuda.synchronize()
-        us = e0.elapsed_time(e1) / (reps * L) * 1e3
-        flop = 2.0 * M * N * K
-        nbytes = M * K * 4 + N * K * 2 + 2 * M * N * 4 + (N * 4 if has_bias else 0)
-        tflops = flop / (us * 1e-6) / 1e12
-        gbps = nbytes / (us * 1e-6) / 1e9
-        t_tensor, t_hbm = flop / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
-        bound = "hbm" if t_hbm > t_tensor else "tensor"
-        entry = {"M": M, "K": K, "N": N, "layers": L, "us_per_layer": round(us, 2), "tflops": round(tflops, 1),
-                 "GBps": round(gbps, 1), "bound": bound,
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            reps = max(3, args.steps)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(reps):
+                    graph.replay()
+                e1.record(stream)
+            torch.cuda.synchronize()
+            del graph
+            us = e0.elapsed_time(e1) / (reps * L) * 1e3
+            flop = 2.0 * M * N * K
+            nbytes = M * K * A.element_size() + N * K * 2 + 2 * M * N * 4 + (N * 4 if has_bias else 0)
+            tflops = flop / (us * 1e-6) / 1e12
+            gbps = nbytes / (us * 1e-6) / 1e9
+            t_tensor, t_hbm = flop / (peaks["bf16_tflops"] * 1e12), nbytes / (peaks["hbm_gbs"] * 1e9)
+            bound = "hbm" if t_hbm > t_tensor else "tensor"
+            e = {"us_per_layer": round(us, 2), "tflops": round(tflops, 1), "GBps": round(gbps, 1), "bound": bound,
                  "frac_of_bound": round((t_hbm if bound == "hbm" else t_tensor) / (us * 1e-6), 4),
-                 "tensor_frac": round(tflops / peaks["bf16_tflops"], 4), "hbm_frac": round(gbps / peaks["hbm_gbs"], 4)}
-        if rank == 0 and not getattr(args, "no_check", False):
-            import oracle as O
-            a0 = A[0, 0].reshape(M, K).cpu().numpy()
-            w0, r0 = W[0].cpu().numpy(), R[0].cpu().numpy()
-            b0 = Bv[0].cpu().numpy() if has_bias else None
-            v = O.parity_verdict(Y[0].cpu().numpy(), O.out_proj(a0, w0, b0, r0),
-                                 O.out_proj(a0, w0, b0, r0, mode=O.MODE_FP64))
-            entry["parity"] = {k: v[k] for k in ("max_abs_err_vs_ggml", "max_abs_err_vs_fp64", "ok")}
+                 "tensor_frac": round(tflops / peaks["bf16_tflops"], 4),
+                 "hbm_frac": round(gbps / peaks["hbm_gbs"], 4)}
+            if rank == 0 and not getattr(args, "no_check", False):
+                import oracle as O
+                a0 = A32[0, 0].reshape(M, K).cpu().numpy()     # the oracle rounds it to f16 itself
+                w0, r0 = W[0].cpu().numpy(), R[0].cpu().numpy()
+                b0 = Bv[0].cpu().numpy() if has_bias else None
+                v = O.parity_verdict(Y[0].cpu().numpy(), O.out_proj(a0, w0, b0, r0),
+                                     O.out_proj(a0, w0, b0, r0, mode=O.MODE_FP64))
+                e["parity"] = {k: v[k] for k in ("max_abs_err_vs_ggml", "max_abs_err_vs_fp64", "ok")}
+            return e
+
+        entry = {"M": M, "K": K, "N": N, "layers": L, "a": "F32 attention result"}
+        entry.update(measure(A32))
+        A16 = A32.half()
+        entry["f16_attention"] = measure(A16)
         res[name] = entry
-        del A, W, R, Y, graph
+        del A32, A16, W, R, Y
         torch.cuda.empty_cache()
     return res
 

@@ -24,7 +24,12 @@
  *   v    [Dv, n_kv, Hkv, B]   same type as k, rows are tokens (not transposed)
  *   mask [n_kv, >= n_q, 1|Hq, 1|B]  F16, additive, -inf = skip; may be NULL
  *   dst  [Dv, Hq, n_q, B]     F32, written by the call (ggml permutes the
- *                             result so one token's heads are contiguous)
+ *                             result so one token's heads are contiguous);
+ *                             F16 is accepted where the tcgen05 kernel runs
+ *                             (n_q * Hq/Hkv >= 64, no mask tensor, no softcap):
+ *                             the F32 result rounded to nearest even, as ggml
+ *                             rounds the activations of the F16 projection
+ *                             weight that consumes it (VTX_ERR_TYPE elsewhere)
  *   O[b,i,h,:] = sum_j softmax_j(scale*q.k_j [softcap] + slope_h*mask[i,j]) v_j
  *
  * All device pointers belong to the caller.  No entry point allocates device
@@ -348,7 +353,9 @@ VTX_API int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t s
  * of h at a stride of block_nb bytes (head i = block i / h, head i % h in
  * it): the rank-major result of a KV-head-split prefill after its
  * all-gather.
- *   attn     F32 [Dv, Hq, n, 1], Dv a multiple of 64
+ *   attn     F32 [Dv, Hq, n, 1], Dv a multiple of 64; or F16 (vtx_flash_attn_ext
+ *            with an F16 dst: the same rounding done once, in the attention
+ *            epilogue; the projection reads it by TMA with no conversion)
  *   w        F16 [K = Dv * Hq, N] (ggml's weight: row r = output feature r)
  *   bias     optional F32 [N]
  *   residual optional F32 [N, n]; may be dst itself

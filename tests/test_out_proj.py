@@ -125,3 +125,56 @@ def test_attention_then_out_proj_matches_oracle_chain():
     v_ = O.parity_verdict(got.cpu().numpy(), O.out_proj(att_g, w, bias, res),
                           O.out_proj(att_f, w, bias, res, mode=O.MODE_FP64))
     assert v_["ok"], v_
+
+
+@pytest.mark.parametrize("n,Hq,Dv,N", [(1500, 20, 64, 1280), (391, 32, 128, 3072), (7, 2, 64, 200)])
+def test_out_proj_f16_attention_is_bit_identical(n, Hq, Dv, N):
+    """An F16 attention output (the rounding ggml applies to the activations,
+    done once upstream) projects bit-identically to the F32 output the
+    kernel rounds itself, and so meets the same parity bar."""
+    import vtx_attn
+    a, w, b, r = _case(11 + n, n, Hq, Dv, N)
+    ta = torch.from_numpy(a).cuda().unsqueeze(0)
+    tw, tb, tr = (torch.from_numpy(x).cuda() for x in (w, b, r))
+    ref = vtx_attn.out_proj(ta, tw, tb, tr)
+    got = vtx_attn.out_proj(ta.half(), tw, tb, tr)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref)
+    _check(got.cpu().numpy(), a, w, b, r, f"f16 attention n={n}")
+
+
+@pytest.mark.parametrize("shape", ["encoder", "decoder_prefill"])
+def test_attention_f16_result_is_the_rounded_f32_result(shape):
+    """vtx_flash_attn_ext with an F16 dst writes exactly the F32 result
+    rounded to nearest even (configs[1] encoder: f16 Q/K/V, 1500 x 20 x 64;
+    configs[2] decoder prefill: F32 Q, causal GQA 32/8 x 128, 391 tokens), and
+    the projection of it equals the projection of the F32 result bit for
+    bit."""
+    import vtx_attn
+    rng = np.random.default_rng(21)
+    if shape == "encoder":
+        n, Hq, Hkv, D, causal, qdt, N = 1500, 20, 20, 64, False, np.float16, 1280
+    else:
+        n, Hq, Hkv, D, causal, qdt, N = 391, 32, 8, 128, True, np.float32, 3072
+    q = torch.from_numpy(rng.standard_normal((1, Hq, n, D)).astype(qdt)).cuda()
+    k = torch.from_numpy(rng.standard_normal((1, Hkv, n, D)).astype(np.float16)).cuda()
+    v = torch.from_numpy(rng.standard_normal((1, Hkv, n, D)).astype(np.float16)).cuda()
+    o32 = vtx_attn.flash_attn_ext(q, k, v, None, D ** -0.5, causal=causal)
+    o16 = vtx_attn.flash_attn_ext(q, k, v, None, D ** -0.5, causal=causal,
+                                  out=torch.empty(o32.shape, dtype=torch.float16, device="cuda"))
+    w = torch.from_numpy((rng.standard_normal((N, Hq * D)) / np.sqrt(Hq * D)).astype(np.float16)).cuda()
+    p32 = vtx_attn.out_proj(o32, w)
+    p16 = vtx_attn.out_proj(o16, w)
+    torch.cuda.synchronize()
+    assert torch.equal(o16, o32.half())
+    assert torch.equal(p16, p32)
+
+
+def test_attention_f16_result_rejected_off_the_tensor_core_path():
+    """A decode call (one query row) has no F16 result: VTX_ERR_TYPE."""
+    import vtx_attn
+    q = torch.randn((1, 32, 1, 128), device="cuda")
+    k = torch.randn((1, 8, 64, 128), device="cuda").half()
+    with pytest.raises(vtx_attn.VtxError) as e:
+        vtx_attn.flash_attn_ext(q, k, k, None, 128 ** -0.5, out=torch.empty((1, 1, 32, 128), device="cuda").half())
+    assert e.value.status == -2

@@ -64,6 +64,7 @@ struct PrefillArgs {
     int *err;
     int lpt;                  // causal launches: longest Q-tile groups first (see the kernel)
     int q_tma;                // f16 Q tiles loaded by TMA through tmQ (else copied by the softmax warps)
+    int o_f16;                // dst is F16 (with o_tma): boxes of 64 halves, rounded to nearest even
 };
 
 template <int D, int NQT> struct PrefillCfg {
@@ -180,7 +181,10 @@ __device__ __forceinline__ void setmaxnreg_dec() { asm volatile("setmaxnreg.dec.
 // non-positive scale (logits formed before the exponent); a template flag so
 // the common instantiation carries none of that code (the softmax loop is
 // fully unrolled, and its size is what the instruction cache sees).
-template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool CSL = false>
+// OF16: the result is written as F16 (rounded to nearest even) through an F16
+// output map, boxes of 64 halves; a template flag so the F32 instantiations
+// carry none of that code.
+template <int D, int NQT, bool HAS_MASK, bool UNFUSED, bool CSL = false, bool OF16 = false>
 __global__ void __launch_bounds__(PrefillCfg<D, NQT>::NTHREADS, 1)
 fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV,
                         const __grid_constant__ CUtensorMap tmO, const __grid_constant__ CUtensorMap tmQ,
@@ -597,10 +601,44 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                 inv = l_run == 0.0f ? 0.0f : 1.0f / l_run;
             }
             const bool store = __all_sync(0xffffffffu, ok) && r == 0 && qt < a.n_tiles_q;
+            if constexpr (OF16) {
+                // F16 result: boxes of [128 rows][64 halves], same swizzle
+#pragma unroll
+                for (int c = 0; c < D / 64; ++c) {
+                    if (ok) {
+                        // 32 columns (four 16-byte chunks of halves) at a time
+                        for (int hh = 0; hh < 2; ++hh) {
+                            uint32_t o[32];
+                            if (t_iters > 0) {
+                                tmem_ld32(o_addr + c * 64 + hh * 32, o);
+                                tmem_ld_wait();
+                            } else {
+#pragma unroll
+                                for (int i = 0; i < 32; ++i) o[i] = 0u;
+                            }
+#pragma unroll
+                            for (int q4 = 0; q4 < 4; ++q4) {
+                                const int q8 = hh * 4 + q4;
+                                *reinterpret_cast<uint4 *>(st + c * 16384 + r * 128 + ((q8 ^ (r & 7)) << 4)) = make_uint4(
+                                    pack_half2(__uint_as_float(o[8 * q4]) * inv, __uint_as_float(o[8 * q4 + 1]) * inv),
+                                    pack_half2(__uint_as_float(o[8 * q4 + 2]) * inv, __uint_as_float(o[8 * q4 + 3]) * inv),
+                                    pack_half2(__uint_as_float(o[8 * q4 + 4]) * inv, __uint_as_float(o[8 * q4 + 5]) * inv),
+                                    pack_half2(__uint_as_float(o[8 * q4 + 6]) * inv, __uint_as_float(o[8 * q4 + 7]) * inv));
+                            }
+                        }
+                    }
+                    fence_proxy_async_smem();
+                    asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // box c of this tile is staged
+                    if (store) {
+                        tma_store_4d(&tmO, st + c * 16384, c * 64, g * a.G, qt * a.tok_per_tile, b);
+                        bulk_commit();
+                    }
+                }
+            }
             // one box at a time: its store is issued as soon as it is staged, so
             // the TMA reads box c while the warpgroup stages box c + 1
 #pragma unroll
-            for (int c = 0; c < D / 32; ++c) {
+            for (int c = 0; c < (OF16 ? 0 : D / 32); ++c) {
                 if (ok) {
                     uint32_t o[32];
                     if (t_iters > 0) {

@@ -23,6 +23,10 @@
 // time, add bias and residual, stage the box in the output map's 128-byte
 // swizzle and write it with a TMA store (two staging buffers in turn).
 //
+// With an F16 A (the attention written with an F16 result, the same rounding
+// done once upstream) the A boxes land by TMA in the MMA's swizzled layout:
+// no conversion warps, half the A bytes, five stages instead of three.
+//
 // A is addressed as [Dv, H_in, n, H_out] so a head-split result gathered by
 // rank (head h = r * H_in + j, each rank's block at its own stride) is read
 // as is.  K = Hq * Dv must be a multiple of 64, Dv a multiple of 64.
@@ -43,9 +47,13 @@ struct OutProjArgs {
     int *err;
 };
 
-struct OutProjCfg {
-    static constexpr int BM = 128, BN = 128, BK = 64, STAGES = 3;
-    static constexpr int A32_BYTES = BM * BK * 4;               // 32 KB F32 box
+// AF16: the attention output is already F16 (the rounding ggml applies to the
+// activations of an F16-weight mat-mul, done in the attention epilogue): A
+// boxes land by TMA in the MMA's 128-byte swizzled layout, no conversion, half
+// the bytes, and twice the stages in flight.
+template <bool AF16 = false> struct OutProjCfgT {
+    static constexpr int BM = 128, BN = 128, BK = 64, STAGES = AF16 ? 5 : 3;
+    static constexpr int A32_BYTES = AF16 ? 0 : BM * BK * 4;    // 32 KB F32 box
     static constexpr int A16_BYTES = BM * BK * 2;               // 16 KB f16, swizzled
     static constexpr int W_BYTES = BN * BK * 2;                 // 16 KB f16, swizzled
     static constexpr int STAGE = A32_BYTES + A16_BYTES + W_BYTES;
@@ -59,13 +67,15 @@ struct OutProjCfg {
     static constexpr int NTHREADS = 192;
     static constexpr int TMEM_COLS = 128;
 };
+using OutProjCfg = OutProjCfgT<false>;
 
-__global__ void __launch_bounds__(OutProjCfg::NTHREADS, 1)
+template <bool AF16>
+__global__ void __launch_bounds__(OutProjCfgT<AF16>::NTHREADS, 1)
 out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmW,
                 const __grid_constant__ CUtensorMap tmY, const __grid_constant__ CUtensorMap tmR,
                 const OutProjArgs a)
 {
-    using C = OutProjCfg;
+    using C = OutProjCfgT<AF16>;
     constexpr int ST = C::STAGES;
     extern __shared__ __align__(1024) char smem_raw[];
     char *smem = reinterpret_cast<char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -120,8 +130,8 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 if (i >= ST && !mbar_wait(&empty[s], (uint32_t)(((i / ST) - 1) & 1), a.err, VTX_KERR_KV)) break;
                 const int k0 = i * C::BK;
                 const int h = k0 / a.Dv, d0 = k0 % a.Dv;
-                mbar_arrive_expect_tx(&full[s], C::A32_BYTES + C::W_BYTES);
-                tma_load_4d(a32(s), &tmA, &full[s], d0, h % a.h_in, m0, h / a.h_in);
+                mbar_arrive_expect_tx(&full[s], (AF16 ? C::A16_BYTES : C::A32_BYTES) + C::W_BYTES);
+                tma_load_4d(AF16 ? a16(s) : a32(s), &tmA, &full[s], d0, h % a.h_in, m0, h / a.h_in);
                 tma_load_2d(wt(s), &tmW, &full[s], k0, n0);
                 issued = i + 1;
             }
@@ -136,7 +146,9 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         bool good = true;
         for (int i = 0; i < nk && good; ++i) {
             const int s = i % ST;
-            good = __all_sync(0xffffffffu, mbar_wait(&conv[s], (uint32_t)((i / ST) & 1), a.err, VTX_KERR_Q));
+            // F32 A: wait for the conversion; F16 A: for the TMA loads themselves
+            good = __all_sync(0xffffffffu, mbar_wait(AF16 ? &full[s] : &conv[s], (uint32_t)((i / ST) & 1), a.err,
+                                                     VTX_KERR_Q));
             if (!good) break;
             tc_fence_after();
             const uint32_t alo = (smem_u32(a16(s)) >> 4) | (1u << 16);
@@ -153,7 +165,7 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
         // =================== convert A, then the epilogue ====================
         const int t = tid - 64;                        // 0..127
         bool ok = true;
-        for (int i = 0; i < nk && ok; ++i) {
+        for (int i = 0; i < (AF16 ? 0 : nk) && ok; ++i) {
             const int s = i % ST;
             ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (uint32_t)((i / ST) & 1), a.err, VTX_KERR_KV));
             if (!ok) break;

@@ -124,10 +124,14 @@ int check_operands(const vtx_tensor *q, const vtx_tensor *k, const vtx_tensor *v
     if (!std::isfinite(p->scale) || !std::isfinite(p->max_bias) || !std::isfinite(p->logit_softcap))
         return VTX_ERR_UNSUPPORTED;
     if (dst) {
-        if (dst->type != VTX_TYPE_F32) return VTX_ERR_TYPE;
+        // F32 is ggml's result type; F16 (the tcgen05 prefill/encoder path only)
+        // is the same result rounded as ggml rounds the activations of the F16
+        // output-projection weight that consumes it
+        if (dst->type != VTX_TYPE_F32 && dst->type != VTX_TYPE_F16) return VTX_ERR_TYPE;
         if (dst->ne[0] != v->ne[0] || dst->ne[1] != q->ne[2] || dst->ne[2] != q->ne[1] || dst->ne[3] != q->ne[3])
             return VTX_ERR_SHAPE;
-        if (dst->nb[0] != 4 || dst->nb[1] % 16 || dst->nb[2] % 16 || dst->nb[3] % 16) return VTX_ERR_STRIDE;
+        if (dst->nb[0] != (size_t)elem_size(dst->type) || dst->nb[1] % 16 || dst->nb[2] % 16 || dst->nb[3] % 16)
+            return VTX_ERR_STRIDE;
     }
     if (mask) {
         if (mask->type != VTX_TYPE_F16) return VTX_ERR_TYPE;
@@ -443,19 +447,21 @@ int encode_q_map(CUtensorMap *m, const void *ptr, int D, int Hq, int n_q, int B,
 // Returns VTX_ERR_STRIDE when the destination cannot be described (base or
 // strides not 16-byte multiples); the caller then uses plain stores.
 int encode_out_map(CUtensorMap *m, void *ptr, int D, int Hq, int n_q, int B, size_t nb1, size_t nb2, size_t nb3,
-                   int G, int tok_per_tile) {
+                   int G, int tok_per_tile, bool f16 = false) {
     if (!g_encode) return VTX_ERR_CUDA;
     if (reinterpret_cast<uintptr_t>(ptr) % 16 || G > 256 || tok_per_tile > 256) return VTX_ERR_STRIDE;
-    const size_t s1 = Hq > 1 ? nb1 : (size_t)D * 4;          // extent-1 dimensions: any legal stride
+    const size_t s1 = Hq > 1 ? nb1 : (size_t)D * (f16 ? 2 : 4);   // extent-1 dimensions: any legal stride
     const size_t s2 = n_q > 1 ? nb2 : s1 * (size_t)Hq;
     const size_t s3 = B > 1 ? nb3 : s2 * (size_t)n_q;
     cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)Hq, (cuuint64_t)n_q, (cuuint64_t)B};
     cuuint64_t strides[3] = {(cuuint64_t)s1, (cuuint64_t)s2, (cuuint64_t)s3};
     for (int i = 0; i < 3; ++i)
         if (strides[i] % 16 || strides[i] == 0) return VTX_ERR_STRIDE;
-    cuuint32_t box[4] = {32, (cuuint32_t)G, (cuuint32_t)tok_per_tile, 1};
+    // one box = 128 bytes of a row (32 floats or 64 halves) x the tile's rows
+    cuuint32_t box[4] = {f16 ? 64u : 32u, (cuuint32_t)G, (cuuint32_t)tok_per_tile, 1};
     cuuint32_t estr[4] = {1, 1, 1, 1};
-    CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims, strides, box, estr,
+    CUresult r = g_encode(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, ptr, dims,
+                          strides, box, estr,
                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? VTX_OK : VTX_ERR_STRIDE;
@@ -653,7 +659,7 @@ bool batch_streaming(const vtx_decode_batch *b) {
     return (b->kv_type == VTX_TYPE_F16 || b->kv_type == VTX_TYPE_F32) && vec == 16;
 }
 
-template <int D, int NQT, bool HM, bool UF, bool CSL = false>
+template <int D, int NQT, bool HM, bool UF, bool CSL = false, bool OF16 = false>
 int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo, const CUtensorMap &mq,
                      const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     using C = PrefillCfg<D, NQT>;
@@ -661,21 +667,26 @@ int launch_prefill_t(const CUtensorMap &mk, const CUtensorMap &mv, const CUtenso
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>,
+        if (cudaFuncSetAttribute(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL, OF16>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) != cudaSuccess)
             return VTX_ERR_CUDA;
         attr_done[dev].store(1, std::memory_order_release);
     }
-    return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL>, grid, dim3(C::NTHREADS), C::SMEM, st, mk, mv, mo,
-                      mq, a);
+    return launch_pdl(fa_prefill_sm100_kernel<D, NQT, HM, UF, CSL, OF16>, grid, dim3(C::NTHREADS), C::SMEM, st, mk,
+                      mv, mo, mq, a);
 }
 
 template <int D, int NQT>
 int launch_prefill_d(bool hm, bool uf, const CUtensorMap &mk, const CUtensorMap &mv, const CUtensorMap &mo,
                      const CUtensorMap &mq, const PrefillArgs &a, dim3 grid, cudaStream_t st) {
     // windowed or multi-wave causal launches (flags only): the causal instantiation
-    if (a.causal && !hm && !uf && (a.lpt || a.window > 0))
-        return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, mq, a, grid, st);
+    const bool csl = a.causal && !hm && !uf && (a.lpt || a.window > 0);
+    if (a.o_f16) {                                            // F16 result: no mask tensor, no softcap
+        if (hm || uf) return VTX_ERR_UNSUPPORTED;
+        return csl ? launch_prefill_t<D, NQT, false, false, true, true>(mk, mv, mo, mq, a, grid, st)
+                   : launch_prefill_t<D, NQT, false, false, false, true>(mk, mv, mo, mq, a, grid, st);
+    }
+    if (csl) return launch_prefill_t<D, NQT, false, false, true>(mk, mv, mo, mq, a, grid, st);
     if (uf) return hm ? launch_prefill_t<D, NQT, true, true>(mk, mv, mo, mq, a, grid, st)
                       : launch_prefill_t<D, NQT, false, true>(mk, mv, mo, mq, a, grid, st);
     return hm ? launch_prefill_t<D, NQT, true, false>(mk, mv, mo, mq, a, grid, st)
@@ -961,14 +972,16 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         a.err = ds->err;
         CUtensorMap mo;
         std::memset(&mo, 0, sizeof(mo));
+        a.o_f16 = dst->type == VTX_TYPE_F16;
         a.o_tma = encode_out_map(&mo, dst->data, g.D, g.Hq, g.n_q, g.B, dst->nb[1], dst->nb[2], dst->nb[3], g.G,
-                                 pp.tok_per_tile) == VTX_OK;
+                                 pp.tok_per_tile, a.o_f16) == VTX_OK;
+        if (a.o_f16 && !a.o_tma) return VTX_ERR_STRIDE;       // F16 results leave by the TMA epilogue only
         CUtensorMap mq;
         std::memset(&mq, 0, sizeof(mq));
         a.q_tma = q->type == VTX_TYPE_F16 && !a.q_quant8 &&
                   encode_q_map(&mq, q->data, g.D, g.Hq, g.n_q, g.B, q->nb[1], q->nb[2], q->nb[3], g.G,
                                pp.tok_per_tile) == VTX_OK;
-        if (!mask && a.q_tma && a.o_tma) {
+        if (!mask && a.q_tma && a.o_tma && !a.o_f16) {
             const SkPlan sp =
                 plan_sk_ranges(g, pp, q->type, params->causal, params->scale, params->logit_softcap, ds->sms);
             if (sp.use) {
@@ -984,6 +997,9 @@ int vtx_flash_attn_ext(const vtx_tensor *q, const vtx_tensor *k, const vtx_tenso
         const dim3 grid = a.lpt ? dim3((unsigned)(pp.n_cta_q * g.Hkv), 1, g.B) : dim3(pp.n_cta_q, g.Hkv, g.B);
         return launch_prefill(g.D, pp.nqt, mask != nullptr, mk, mv, mo, mq, a, grid, st);
     }
+
+    // F16 results come only from the tcgen05 kernel's TMA epilogue (above)
+    if (dst->type != VTX_TYPE_F32) return VTX_ERR_TYPE;
 
     // ---- split-KV path ---------------------------------------------------------
     const SplitPlan sp = plan_split(g, ds->sms, g.n_kv, false);
@@ -1240,7 +1256,10 @@ int vtx_encoder_stitch(const void *src, size_t src_chunk_bytes, size_t src_row_b
 int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
     if (!p || !p->attn || !p->w || !p->dst) return VTX_ERR_NULL;
     const vtx_tensor &A = *p->attn, &W = *p->w, &Y = *p->dst;
-    if (A.type != VTX_TYPE_F32 || W.type != VTX_TYPE_F16 || Y.type != VTX_TYPE_F32) return VTX_ERR_TYPE;
+    if ((A.type != VTX_TYPE_F32 && A.type != VTX_TYPE_F16) || W.type != VTX_TYPE_F16 || Y.type != VTX_TYPE_F32)
+        return VTX_ERR_TYPE;
+    const bool af16 = A.type == VTX_TYPE_F16;
+    const size_t aes = af16 ? 2 : 4;
     const int64_t Dv = A.ne[0], Hq = A.ne[1], n = A.ne[2];
     if (A.ne[3] != 1 || Dv <= 0 || Dv % 64 || Hq <= 0 || n < 0) return VTX_ERR_SHAPE;
     const int64_t K = Dv * Hq, N = W.ne[1];
@@ -1252,7 +1271,7 @@ int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
     const int hb = p->head_block > 0 ? p->head_block : (int)Hq;
     if (Hq % hb) return VTX_ERR_SHAPE;
     const int h_out = (int)(Hq / hb);
-    if (A.nb[0] != 4 || W.nb[0] != 2 || Y.nb[0] != 4) return VTX_ERR_STRIDE;
+    if (A.nb[0] != aes || W.nb[0] != 2 || Y.nb[0] != 4) return VTX_ERR_STRIDE;
     const size_t outer = h_out > 1 ? p->block_nb : A.nb[1] * (size_t)hb;
     const uintptr_t al = reinterpret_cast<uintptr_t>(A.data) | reinterpret_cast<uintptr_t>(W.data) |
                          reinterpret_cast<uintptr_t>(Y.data) | (uintptr_t)A.nb[1] | (uintptr_t)A.nb[2] |
@@ -1282,13 +1301,15 @@ int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
     {
         // A: [Dv, heads in a block, tokens, blocks], one box = 64 columns of one head x 128 tokens
         cuuint64_t dims[4] = {(cuuint64_t)Dv, (cuuint64_t)hb, (cuuint64_t)n, (cuuint64_t)h_out};
-        cuuint64_t strides[3] = {(cuuint64_t)(hb > 1 ? A.nb[1] : Dv * 4), (cuuint64_t)(n > 1 ? A.nb[2] : 16),
+        cuuint64_t strides[3] = {(cuuint64_t)(hb > 1 ? A.nb[1] : Dv * aes), (cuuint64_t)(n > 1 ? A.nb[2] : 16),
                                  (cuuint64_t)outer};
         for (int i = 0; i < 3; ++i)
             if (strides[i] == 0 || strides[i] % 16 || strides[i] >= (1ULL << 40)) return VTX_ERR_STRIDE;
         cuuint32_t box[4] = {64, 1, 128, 1}, estr[4] = {1, 1, 1, 1};
-        if (g_encode(&ma, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A.data, dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+        // F16 A lands in the MMA's 128-byte swizzle directly; F32 A unswizzled for the conversion
+        if (g_encode(&ma, af16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, A.data, dims,
+                     strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     af16 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return VTX_ERR_STRIDE;
     }
@@ -1318,8 +1339,10 @@ int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(out_proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, OutProjCfg::SMEM) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(out_proj_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 OutProjCfgT<false>::SMEM) != cudaSuccess ||
+            cudaFuncSetAttribute(out_proj_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 OutProjCfgT<true>::SMEM) != cudaSuccess)
             return VTX_ERR_CUDA;
         attr_done[dev].store(1, std::memory_order_release);
     }
@@ -1328,8 +1351,10 @@ int vtx_attn_out_proj(const vtx_out_proj_args *p, void *stream) {
     a.bias = bias; a.res = res; a.res_nb1 = res_nb1; a.err = ds->err;
     const dim3 grid((unsigned)((n + OutProjCfg::BM - 1) / OutProjCfg::BM), (unsigned)((N + OutProjCfg::BN - 1) / OutProjCfg::BN));
     if (grid.y > 65535) return VTX_ERR_UNSUPPORTED;
-    return launch_pdl(out_proj_kernel, grid, dim3(OutProjCfg::NTHREADS), OutProjCfg::SMEM,
-                      static_cast<cudaStream_t>(stream), ma, mw, my, mr, a);
+    return af16 ? launch_pdl(out_proj_kernel<true>, grid, dim3(OutProjCfgT<true>::NTHREADS), OutProjCfgT<true>::SMEM,
+                             static_cast<cudaStream_t>(stream), ma, mw, my, mr, a)
+                : launch_pdl(out_proj_kernel<false>, grid, dim3(OutProjCfg::NTHREADS), OutProjCfg::SMEM,
+                             static_cast<cudaStream_t>(stream), ma, mw, my, mr, a);
 }
 
 int vtx_read_device_error(void *stream) {

@@ -475,13 +475,15 @@ def out_proj(attn: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] =
     """vtx_attn_out_proj: out = residual + bias + f16(attn) @ w^T (f32 accumulate),
     the output projection after the attention node (src/voxtral.cpp:1612-1617,
     :1804-1809).  attn: (1, n, Hq, Dv) float32 as flash_attn_ext returns it,
-    any strides, read in place; or (1, n, R, h, Dv), the rank-major result of
-    shard.head_split_prefill (head = r * h + j).  w: (N, Hq * Dv) float16;
+    any strides, read in place, or float16 (flash_attn_ext with a float16
+    `out`: the same rounding, done in the attention epilogue); or
+    (1, n, R, h, Dv), the rank-major result of shard.head_split_prefill
+    (head = r * h + j).  w: (N, Hq * Dv) float16;
     bias: (N,) float32 or None; residual: (n, N) float32 or None (it may be
     `out`).  Returns out (n, N) float32."""
-    if attn.dtype != torch.float32 or w.dtype != torch.float16:
-        raise VtxError(-2, "attn must be float32 and w float16")
-    es = 4
+    if attn.dtype not in (torch.float32, torch.float16) or w.dtype != torch.float16:
+        raise VtxError(-2, "attn must be float32 or float16 and w float16")
+    es = attn.element_size()
     if attn.dim() == 4:
         _, n, Hq, Dv = attn.shape
         head_nb, tok_nb = attn.stride(2) * es, attn.stride(1) * es
@@ -498,7 +500,7 @@ def out_proj(attn: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] =
     N, K = w.shape
     if out is None:
         out = torch.empty((n, N), dtype=torch.float32, device=attn.device)
-    a = _raw_tensor(F32, [Dv, Hq, n, 1], [4, head_nb, tok_nb, tok_nb * n], attn.data_ptr())
+    a = _raw_tensor(F32 if es == 4 else F16, [Dv, Hq, n, 1], [es, head_nb, tok_nb, tok_nb * n], attn.data_ptr())
     wd = _raw_tensor(F16, [K, N, 1, 1], [2, w.stride(0) * 2], w.data_ptr())
     yd = _raw_tensor(F32, [N, n, 1, 1], [4, out.stride(0) * 4], out.data_ptr())
     bd = _raw_tensor(F32, [N, 1, 1, 1], [4], bias.data_ptr()) if bias is not None else None
