@@ -52,14 +52,20 @@ struct OutProjArgs {
 // boxes land by TMA in the MMA's 128-byte swizzled layout, no conversion, half
 // the bytes, and twice the stages in flight.
 template <bool AF16 = false> struct OutProjCfgT {
-    static constexpr int BM = 128, BN = 128, BK = 64, STAGES = AF16 ? 5 : 3;
+    static constexpr int BM = 128, BN = 128, BK = 64, STAGES = AF16 ? 4 : 3;
     static constexpr int A32_BYTES = AF16 ? 0 : BM * BK * 4;    // 32 KB F32 box
     static constexpr int A16_BYTES = BM * BK * 2;               // 16 KB f16, swizzled
     static constexpr int W_BYTES = BN * BK * 2;                 // 16 KB f16, swizzled
     static constexpr int STAGE = A32_BYTES + A16_BYTES + W_BYTES;
     static constexpr int OUT_BOX = BM * 32 * 4;                 // [128 tokens][32 floats]
     static constexpr int OUT_OFF = STAGES * STAGE;
-    static constexpr int BAR_OFF = OUT_OFF + 2 * OUT_BOX;
+    // AF16: the residual tile has its own buffer and is fetched while the K
+    // loop runs (the conversion warps are idle); F32 A: it is fetched into the
+    // freed stages once every MMA has retired.  The tile's bias columns are
+    // staged in shared memory before the epilogue in both cases.
+    static constexpr int RES_OFF = OUT_OFF + 2 * OUT_BOX;
+    static constexpr int BIAS_OFF = RES_OFF + (AF16 ? BN / 32 * OUT_BOX : 0);
+    static constexpr int BAR_OFF = BIAS_OFF + BN * 4;
     // full[S], conv[S], empty[S], acc, res_full
     static constexpr int NBARS = 3 * STAGES + 2;
     static_assert(BN / 32 * OUT_BOX <= STAGES * STAGE, "the residual tile fits in the freed stages");
@@ -188,22 +194,31 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
             __syncwarp();
             if (lane == 0) mbar_arrive(&conv[s]);
         }
+        const bool leader = warp == 2 && lane == 0;
+        char *res_tile = AF16 ? smem + C::RES_OFF : smem;
+        if (AF16 && a.res && leader) {                 // the residual tile, while the K loop runs
+            mbar_arrive_expect_tx(res_full, C::BN / 32 * C::OUT_BOX);
+#pragma unroll
+            for (int c = 0; c < C::BN / 32; ++c) tma_load_2d(res_tile + c * C::OUT_BOX, &tmR, res_full, n0 + c * 32, m0);
+        }
+        float *bias_s = reinterpret_cast<float *>(smem + C::BIAS_OFF);
+        if (a.bias) bias_s[t] = n0 + t < a.N ? __ldg(a.bias + n0 + t) : 0.0f;
         if (ok) ok = __all_sync(0xffffffffu, mbar_wait(acc, 0, a.err, VTX_KERR_O));
         tc_fence_after();
         // this warp's TMEM lanes: tokens 32q .. 32q + 31 of the tile
         const int q = warp & 3, r = 32 * q + lane;
         const uint32_t t_row = tmem + ((uint32_t)(32 * q) << 16);
-        const bool leader = warp == 2 && lane == 0;
-        // Every MMA has retired and every load has landed (the MMA consumed
-        // them), so the stage buffers are free: the whole residual tile is
-        // fetched into them at once, in the output boxes' swizzled layout.
-        char *res_tile = smem;
-        if (a.res && leader && ok) {
+        // F32 A: every MMA has retired and every load has landed (the MMA
+        // consumed them), so the stage buffers are free: the whole residual
+        // tile is fetched into them at once, in the output boxes' swizzled layout.
+        if (!AF16 && a.res && leader && ok) {
             mbar_arrive_expect_tx(res_full, C::BN / 32 * C::OUT_BOX);
 #pragma unroll
             for (int c = 0; c < C::BN / 32; ++c) tma_load_2d(res_tile + c * C::OUT_BOX, &tmR, res_full, n0 + c * 32, m0);
         }
-        if (a.res && ok) ok = __all_sync(0xffffffffu, mbar_wait(res_full, 0, a.err, VTX_KERR_O));
+        // (AF16: waited even after a failed wait above: the load was issued and
+        // must land before the CTA's shared memory is released)
+        if (a.res && (ok || AF16)) ok = __all_sync(0xffffffffu, mbar_wait(res_full, 0, a.err, VTX_KERR_O)) && ok;
         for (int c = 0; c < C::BN / 32; ++c) {
             char *stg = smem + C::OUT_OFF + (c & 1) * C::OUT_BOX;
             if (c >= 2 && leader) bulk_wait_read<1>();   // the store that used this buffer has read it
@@ -216,10 +231,9 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 float f[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
-                if (a.bias) {
+                if (a.bias) {                   // staged above; 0 past the tensor
 #pragma unroll
-                    for (int i = 0; i < 32; ++i)
-                        if (col0 + i < a.N) f[i] += __ldg(a.bias + col0 + i);
+                    for (int i = 0; i < 32; ++i) f[i] += bias_s[c * 32 + i];
                 }
                 if (a.res) {                    // rows / columns past the tensor read as zeros
                     const char *rb = res_tile + c * C::OUT_BOX + r * 128;
