@@ -25,7 +25,8 @@
 //
 // With an F16 A (the attention written with an F16 result, the same rounding
 // done once upstream) the A boxes land by TMA in the MMA's swizzled layout:
-// no conversion warps, half the A bytes, five stages instead of three.
+// no conversion warps, half the A bytes, four stages instead of three and the
+// residual tile fetched into its own buffer while the K loop runs.
 //
 // A is addressed as [Dv, H_in, n, H_out] so a head-split result gathered by
 // rank (head h = r * H_in + j, each rank's block at its own stride) is read
@@ -50,7 +51,7 @@ struct OutProjArgs {
 // AF16: the attention output is already F16 (the rounding ggml applies to the
 // activations of an F16-weight mat-mul, done in the attention epilogue): A
 // boxes land by TMA in the MMA's 128-byte swizzled layout, no conversion, half
-// the bytes, and twice the stages in flight.
+// the bytes per stage.
 template <bool AF16 = false> struct OutProjCfgT {
     static constexpr int BM = 128, BN = 128, BK = 64, STAGES = AF16 ? 4 : 3;
     static constexpr int A32_BYTES = AF16 ? 0 : BM * BK * 4;    // 32 KB F32 box
@@ -90,7 +91,7 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
     uint64_t *conv = full + ST;             // [ST] A16 of a stage written (4 warp arrivals)
     uint64_t *empty = conv + ST;            // [ST] the stage's MMAs retired
     uint64_t *acc = empty + ST;             // every MMA retired
-    uint64_t *res_full = acc + 1;           // the residual tile landed (in the freed stage buffers)
+    uint64_t *res_full = acc + 1;           // the residual tile landed
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(res_full + 1);
     auto a32 = [&](int s) { return smem + s * C::STAGE; };
     auto a16 = [&](int s) { return smem + s * C::STAGE + C::A32_BYTES; };
@@ -227,7 +228,6 @@ out_proj_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__
                 uint32_t v[32];
                 tmem_ld32(t_row + c * 32, v);
                 tmem_ld_wait();
-                const int col0 = n0 + c * 32;
                 float f[32];
 #pragma unroll
                 for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
