@@ -89,7 +89,7 @@ template <int D, int NQT> struct PrefillCfg {
     // while the softmax of the current one is still computing.  Otherwise P
     // aliases S and the next S waits for P V.
     static constexpr bool LA = !ROWSUM && NQT * (128 + 64 + D) <= 512;
-    static constexpr int NBARS = 1 + 3 * STAGES + 4 * NQT + 1;
+    static constexpr int NBARS = 1 + 3 * STAGES + 4 * NQT + 1 + NQT;
     static constexpr int SMEM = BAR_OFF + NBARS * 8 + 16 + 1024;   // +1024 alignment slack
     static constexpr int NTHREADS = 128 * NQT + 128;
     static constexpr int TMA_WARP = 4 * NQT, MMA_WARP = 4 * NQT + 1;
@@ -203,7 +203,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     uint64_t *pv_done = s_free + NQT;              // LA: O_t += P_t V done, P_t may be rewritten
     uint64_t *o_full = pv_done + NQT;
     uint64_t *v_full = o_full + 1;                 // V_j of a stage landed
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(v_full + C::STAGES);
+    uint64_t *o_tile = v_full + C::STAGES;         // EARLY_O: every S and tile t's last P V retired
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(o_tile + NQT);
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     // CSL: the instantiation for causal launches with the causal/window flags
@@ -217,6 +218,13 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     //     launch, grid (groups, Hkv, B) with a head's CTAs adjacent;
     //   * each Q tile runs only over its own key tiles (tile_iters below),
     //     not over the union of the CTA's tiles.
+    // EARLY_O (P aliasing S, every Q tile over the same key tiles): tile t's
+    // write-back starts when its own last P V has retired (o_tile[t]), while
+    // the other tile's last softmax and P V still run.  The MMA issuer puts
+    // every S of the CTA before the first tile's last P V, so by then the Q
+    // tiles and the K ring -- tile 0's and tile 1's staging -- are idle; the
+    // pending P V reads only the V ring and the constant block.
+    constexpr bool EARLY_O = !C::LA && !CSL;
     const int b = blockIdx.z;
     const bool lpt = CSL && a.lpt;
     const int g = lpt ? (int)(blockIdx.x % a.Hkv) : (int)blockIdx.y;
@@ -272,6 +280,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             mbar_init(&pv_done[t], 1);
         }
         mbar_init(o_full, 1);
+        for (int t = 0; t < NQT; ++t) mbar_init(&o_tile[t], 1);
         fence_mbar_init();
     }
     if (warp == C::MMA_WARP) {             // MMA warp owns the TMEM allocation
@@ -578,9 +587,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (lane == 0) mbar_arrive(&p_full[t]);   // per-warp arrival
         }
         // ---- epilogue: O / l -> dst ------------------------------------------
-        if (ok && n_iter > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_full, 0, a.err, VTX_KERR_O));
+        if (ok && n_iter > 0)
+            ok = __all_sync(0xffffffffu, mbar_wait(EARLY_O ? &o_tile[t] : o_full, 0, a.err, VTX_KERR_O));
         // After o_full every MMA has retired and every TMA load has landed, so
-        // the Q tiles and the K/V ring are free to stage O.
+        // the Q tiles and the K/V ring are free to stage O; after o_tile[t]
+        // (EARLY_O) every S has, so the Q tiles and the K ring are.
         if (a.o_tma) {
             // Staged as D/32 boxes of [128 rows][32 floats] per tile in the 128-byte
             // swizzled layout of the output tensor map (conflict-free: a row's
@@ -854,6 +865,7 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                         mma_commit_w(lead, &kv_empty[st]);
                     }
                 }
+                uint32_t o_done = 0;                   // EARLY_O: tiles whose o_tile was committed
                 for (int it = 0; !C::LA && it <= n_iter && good; ++it) {
                     const int st = it % C::STAGES;
                     const int pst = (it + C::STAGES - 1) % C::STAGES;
@@ -880,6 +892,10 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                             }
                             tc_fence_after();
                             issue_pv(t, pst, pi > t_lo ? 1u : 0u);
+                            if (EARLY_O && pi == t_hi - 1) {   // tile t's O is final
+                                mma_commit_w(lead, &o_tile[t]);
+                                o_done |= 1u << t;
+                            }
                         }
                         if (it >= t_lo && it < t_hi) {
                             if (!k_ready) {
@@ -896,6 +912,11 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     }
                     if (!good) break;
                     if (it > 0) mma_commit_w(lead, &kv_empty[pst]);
+                }
+                if (EARLY_O) {                         // a failed wait above: release the write-back
+#pragma unroll
+                    for (int t = 0; t < NQT; ++t)
+                        if (!((o_done >> t) & 1u)) mma_commit_w(lead, &o_tile[t]);
                 }
                 mma_commit_w(lead, o_full);
                 // every MMA of this CTA must be retired before TMEM is released
