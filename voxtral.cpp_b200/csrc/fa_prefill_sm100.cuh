@@ -218,13 +218,17 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
     //     launch, grid (groups, Hkv, B) with a head's CTAs adjacent;
     //   * each Q tile runs only over its own key tiles (tile_iters below),
     //     not over the union of the CTA's tiles.
-    // EARLY_O (P aliasing S, every Q tile over the same key tiles): tile t's
-    // write-back starts when its own last P V has retired (o_tile[t]), while
-    // the other tile's last softmax and P V still run.  The MMA issuer puts
-    // every S of the CTA before the first tile's last P V, so by then the Q
-    // tiles and the K ring -- tile 0's and tile 1's staging -- are idle; the
-    // pending P V reads only the V ring and the constant block.
-    constexpr bool EARLY_O = !C::LA && !CSL;
+    // EARLY_O (P aliasing S): tile t's write-back starts when its own last
+    // P V has retired (o_tile[t]), while the other tile's last softmax and
+    // P V still run.  When every Q tile walks the same key tiles, the MMA
+    // issuer puts every S of the CTA before the first tile's last P V, so by
+    // then the Q tiles and the K ring -- tile 0's and tile 1's staging -- are
+    // idle; the pending P V reads only the V ring and the constant block.
+    // CSL (a tile's own key range, the later tile's reaching further): the
+    // later tile may still run S over Q_1 and the K ring, so tile 0 stages in
+    // its own Q tile, one TILE_BYTES group of boxes at a time (TMA
+    // write-back only; the row-store write-back waits for every MMA).
+    constexpr bool EARLY_O = !C::LA;
     const int b = blockIdx.z;
     const bool lpt = CSL && a.lpt;
     const int g = lpt ? (int)(blockIdx.x % a.Hkv) : (int)blockIdx.y;
@@ -587,8 +591,9 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             if (lane == 0) mbar_arrive(&p_full[t]);   // per-warp arrival
         }
         // ---- epilogue: O / l -> dst ------------------------------------------
+        const bool early_o = EARLY_O && (!CSL || a.o_tma);
         if (ok && n_iter > 0)
-            ok = __all_sync(0xffffffffu, mbar_wait(EARLY_O ? &o_tile[t] : o_full, 0, a.err, VTX_KERR_O));
+            ok = __all_sync(0xffffffffu, mbar_wait(early_o ? &o_tile[t] : o_full, 0, a.err, VTX_KERR_O));
         // After o_full every MMA has retired and every TMA load has landed, so
         // the Q tiles and the K/V ring are free to stage O; after o_tile[t]
         // (EARLY_O) every S has, so the Q tiles and the K ring are.
@@ -599,7 +604,8 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             // TMA store per box; rows past the end of the sequence are clipped by
             // the hardware.
             static_assert(NQT * (D / 32) * 16384 <= C::BAR_OFF, "O staging overlaps the barriers");
-            char *st = smem + C::Q_OFF + t * (D / 32) * 16384;
+            const bool own_q = CSL && EARLY_O && NQT == 2 && t == 0;
+            char *st = own_q ? smem + C::Q_OFF : smem + C::Q_OFF + t * (D / 32) * 16384;
             float inv = 0.0f;
             if (ok) {
                 tc_fence_after();
@@ -650,6 +656,12 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
             // the TMA reads box c while the warpgroup stages box c + 1
 #pragma unroll
             for (int c = 0; c < (OF16 ? 0 : D / 32); ++c) {
+                constexpr int GROUP = C::TILE_BYTES / 16384;           // boxes in one Q tile
+                const int slot = own_q ? c % GROUP : c;
+                if (own_q && c > 0 && c % GROUP == 0) {                // the group's stores have read it
+                    if (store) bulk_wait_read_all();
+                    asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");
+                }
                 if (ok) {
                     uint32_t o[32];
                     if (t_iters > 0) {
@@ -661,14 +673,14 @@ fa_prefill_sm100_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_co
                     }
 #pragma unroll
                     for (int q4 = 0; q4 < 8; ++q4)
-                        *reinterpret_cast<float4 *>(st + c * 16384 + r * 128 + ((q4 ^ (r & 7)) << 4)) =
+                        *reinterpret_cast<float4 *>(st + slot * 16384 + r * 128 + ((q4 ^ (r & 7)) << 4)) =
                             make_float4(__uint_as_float(o[4 * q4]) * inv, __uint_as_float(o[4 * q4 + 1]) * inv,
                                         __uint_as_float(o[4 * q4 + 2]) * inv, __uint_as_float(o[4 * q4 + 3]) * inv);
                 }
                 fence_proxy_async_smem();
                 asm volatile("bar.sync %0, 128;" ::"r"(1 + t) : "memory");   // box c of this tile is staged
                 if (store) {
-                    tma_store_4d(&tmO, st + c * 16384, c * 32, g * a.G, qt * a.tok_per_tile, b);
+                    tma_store_4d(&tmO, st + slot * 16384, c * 32, g * a.G, qt * a.tok_per_tile, b);
                     bulk_commit();
                 }
             }
