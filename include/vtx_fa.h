@@ -266,6 +266,13 @@ VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_l
  *   and the pointer arrays may be read while the kernel launched just before
  *   still runs (they must be complete before it); only q, k and v are waited
  *   for.  early = 0 reads nothing before that kernel completes.
+ * - max_kv_len: a bound on every kv_len[s] for the calls made with these
+ *   arguments.  It sizes the workspace and picks the key splits: when few are
+ *   needed (short bounds) the splits of a (stream, KV head) run as one
+ *   thread-block cluster and merge through distributed shared memory, else
+ *   they merge through the workspace.  A longer kv_len[s] still gives the
+ *   exact result, over the bound's splits.  The first call on a device
+ *   queries the device's cluster capacity once (make it before a capture).
  * - workspace: vtx_decode_layer_workspace(args) bytes, 256-byte aligned:
  *   split partials and one arrival counter per stream and KV head.  Zero it
  *   once before the first call (cudaMemset); every completed call leaves it
@@ -276,7 +283,7 @@ VTX_API int vtx_decode_advance(int32_t *positions, int32_t *slots, int32_t *kv_l
 typedef struct {
     int32_t n_seq, n_head_q, n_head_kv, head_dim;
     int32_t kv_type;                    /* VTX_TYPE_F16 or VTX_TYPE_Q8_0 */
-    int32_t max_kv_len;                 /* bound on every kv_len[s] (sizes the key splits) */
+    int32_t max_kv_len;                 /* bound on every kv_len[s] (picks the key splits) */
     float freq_base;                    /* RoPE base (voxtral.cpp: 1e6) */
     float scale;                        /* softmax scale, 1/sqrt(head_dim) */
     const float *q; size_t q_nb1;

@@ -31,10 +31,11 @@ def _views(host_k, host_v, n, Hkv, D, hb, kv_type):
     return kk.transpose(1, 0, 2)[None], vv.transpose(1, 0, 2)[None]
 
 
-def run_layer(kv_type, lens, Hq=32, Hkv=8, D=128, W=8192, seed=0, early=False, steps=1):
+def run_layer(kv_type, lens, Hq=32, Hkv=8, D=128, W=8192, seed=0, early=False, steps=1, bound=None):
     """lens[s]: tokens in stream s once this step's token is appended.  Runs
     `steps` consecutive calls (the counters advanced on the host between
-    them) and checks each against the oracle."""
+    them) and checks each against the oracle.  bound: the plan's max_kv_len
+    (default: the ring's rows)."""
     import vtx_attn
     rng = np.random.default_rng(seed)
     S = len(lens)
@@ -56,8 +57,8 @@ def run_layer(kv_type, lens, Hq=32, Hkv=8, D=128, W=8192, seed=0, early=False, s
     positions = torch.tensor([n - 1 for n in lens], dtype=torch.int32, device="cuda")
     slots = torch.tensor([(n - 1) % W for n in lens], dtype=torch.int32, device="cuda")
     kv_len = torch.tensor([min(n, W) for n in lens], dtype=torch.int32, device="cuda")
-    plan = vtx_attn.DecodeLayerPlan(kc, vc, positions, slots, kv_len, Hq, Hkv, D, kv_type, row, W, D ** -0.5,
-                                    1e6, early=early)
+    plan = vtx_attn.DecodeLayerPlan(kc, vc, positions, slots, kv_len, Hq, Hkv, D, kv_type, row,
+                                    W if bound is None else bound, D ** -0.5, 1e6, early=early)
     for step in range(steps):
         q = rng.standard_normal((S, Hq, D)).astype(np.float32)
         k = rng.standard_normal((S, Hkv, D)).astype(np.float32)
@@ -132,3 +133,21 @@ def test_early_ring_fill(kv):
     result and the written row are the same."""
     run_layer(kv, [2500, 9], seed=41 + kv, early=True, steps=2)
 
+
+
+@pytest.mark.parametrize("kv,n,bound", [(O.F16, 391, 1024), (O.F16, 1000, 1024), (O.Q8_0, 600, 2048),
+                                        (O.Q8_0, 2000, 2048), (O.Q8_0, 3000, 1024)],
+                         ids=["f16-391", "f16-1000", "q8_0-600", "q8_0-2000", "q8_0-3000-past-bound"])
+def test_cluster_merge(kv, n, bound):
+    """A tighter key bound plans few splits (at most 12 here) merged through
+    distributed shared memory: the splits of each KV head are the CTAs of one
+    thread-block cluster.  A cache longer than the bound stays correct (its
+    splits are capped, each longer).  Two calls in a row."""
+    run_layer(kv, [n], seed=90 + n + kv, steps=2, bound=bound)
+
+
+@pytest.mark.parametrize("kv", [O.F16, O.Q8_0], ids=["f16", "q8_0"])
+def test_cluster_merge_ragged(kv):
+    """Two streams under one bound: one with a single split (its cluster's
+    other CTAs leave at once), one merged in the cluster."""
+    run_layer(kv, [40, 900], seed=95 + kv, steps=2, bound=1024, early=True)

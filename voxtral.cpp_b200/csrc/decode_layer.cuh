@@ -25,11 +25,17 @@
 //             dequantised to f16, O^T += V^T P^T (the arithmetic of the
 //             streaming decode kernels for these cache types);
 //   merge     the W warps' softmax states in shared memory, then, with more
-//             than one split, a partial (O, m, l) per CTA; the last CTA of a
-//             (stream, KV head) to arrive -- counted by one atomic increment
-//             that wraps to zero on the last arrival, so the workspace needs
-//             zeroing once and every call leaves it zeroed -- merges the
-//             partials and writes ggml's F32 row.
+//             than one split, a partial (O, m, l) per CTA, merged either
+//             (CL) through distributed shared memory: the splits of a
+//             (stream, KV head) are the CTAs of one thread-block cluster, two
+//             cluster barriers, each CTA folding every split's partial for
+//             its share of the rows -- for launches with few splits, whose
+//             small clusters let the next layer's CTAs become resident early;
+//             or through global memory: the last CTA of a (stream, KV head)
+//             to arrive -- counted by one atomic increment that wraps to zero
+//             on the last arrival, so the workspace needs zeroing once and
+//             every call leaves it zeroed -- merges the partials and writes
+//             ggml's F32 row.
 //
 // Numerics are those of the separate calls: Q rotated in f32 then rounded to
 // half (F16 cache) or quantised per 32 values (Q8_0 cache), f32 scores and
@@ -106,6 +112,11 @@ template <int KVT> struct LayerCfg {
     static constexpr int ST_F = ST_ML + W * GMAX * 8;          // [W][GMAX] merge factors, then [GMAX] 1/L or L
     static constexpr int GRP_OFF = ST_F + (W + 1) * GMAX * 4;  // split merge: [NT] float4 acc + (m, l)
     static_assert(GRP_OFF + NT * 24 <= W * RING, "merge buffers overlap the barriers");
+    // cluster merge (CL): this split's O rows and (m, l) at GRP_OFF; at most
+    // CLMAX splits (the portable cluster size)
+    static constexpr int CLMAX = 8;
+    static_assert(GRP_OFF + GMAX * D * 4 + GMAX * 8 <= W * RING, "cluster partial overlaps the barriers");
+    static_assert(GRP_OFF % 16 == 0, "16-byte cluster loads of the partial");
 };
 
 // Arrival on a split counter: old value returned, the counter wraps to 0 on
@@ -117,7 +128,7 @@ __device__ __forceinline__ unsigned arrive_inc_acq_rel(unsigned *p, unsigned las
     return old;
 }
 
-template <int KVT>
+template <int KVT, bool CL>
 __global__ void __launch_bounds__(LayerCfg<KVT>::NT, LayerCfg<KVT>::MINB)
 fa_decode_layer_kernel(const DecodeLayerArgs a)
 {
@@ -147,7 +158,17 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
     const int nsp = max(1, (kv_len + chunk - 1) / chunk);
     const int kb = sp * chunk;
     const int ke = min(kb + chunk, kv_len);
-    if (sp >= nsp) return;                                     // past the stream's keys: not merged
+    if (sp >= nsp) {                                           // past the stream's keys: not merged
+        if constexpr (CL) {
+            if (nsp > 1) {                                     // the cluster's two barriers, no partial
+                cluster_arrive();
+                cluster_wait();
+                cluster_arrive();
+                cluster_wait();
+            }
+        }
+        return;
+    }
     const char *kbase = static_cast<const char *>(kp0) + (long long)g * C::HB;
     const char *vbase = static_cast<const char *>(vp0) + (long long)g * C::HB;
     // Q8_0 rows (136 B) of odd heads sit 8 bytes past a 16-byte boundary: copy
@@ -422,6 +443,8 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
     // its W lanes (W divides 32)
     const long long work = ((long long)b * a.Hkv + g) * a.n_splits + sp;
     float *st_f = reinterpret_cast<float *>(smem + C::ST_F);
+    float *cl_o = reinterpret_cast<float *>(smem + C::GRP_OFF);                        // CL: this split's
+    float2 *cl_ml = reinterpret_cast<float2 *>(smem + C::GRP_OFF + C::GMAX * D * 4);   // O rows, (m, l)
     static_assert(W <= 32 && (W & (W - 1)) == 0 && C::GMAX * W % 32 == 0 && C::GMAX * W <= C::NT,
                   "a row's W lanes inside one warp, whole warps");
     if (threadIdx.x < C::GMAX * W) {
@@ -438,7 +461,10 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
             st_f[w * C::GMAX + r] = f;
             if (w == 0) {
                 st_f[W * C::GMAX + r] = nsp == 1 ? (L == 0.f ? 0.f : 1.f / L) : L;
-                if (nsp > 1) reinterpret_cast<float2 *>(a.part_ml)[work * a.G + r] = make_float2(M, L);
+                if (nsp > 1) {
+                    if constexpr (CL) cl_ml[r] = make_float2(M, L);
+                    else reinterpret_cast<float2 *>(a.part_ml)[work * a.G + r] = make_float2(M, L);
+                }
             }
         }
     }
@@ -453,9 +479,58 @@ fa_decode_layer_kernel(const DecodeLayerArgs a)
         }
         const float x = st_f[W * C::GMAX + r];
         if (nsp == 1) a.dst[(long long)b * a.dst_nb1 + (long long)(g * a.G + r) * D + d] = O * x;
+        else if constexpr (CL) cl_o[r * D + d] = O;
         else a.part_o[(work * a.G + r) * D + d] = O;
     }
     if (nsp == 1) return;
+
+    if constexpr (CL) {
+        // ---- cluster merge: CTA sp folds the partials of all nsp splits
+        //      (distributed shared memory, split order) for its share of the
+        //      G x D/4 float4 outputs
+        cluster_arrive();
+        cluster_wait();                                        // every split's partial is in place
+        const int items = a.G * (D / 4);
+        const int per = (items + nsp - 1) / nsp;
+        const int item = sp * per + (int)threadIdx.x;
+        if ((int)threadIdx.x < per && item < items) {
+            const int r = item / (D / 4), c = item % (D / 4);
+            const uint32_t o_loc = smem_u32(cl_o + r * D + 4 * c);
+            const uint32_t ml_loc = smem_u32(cl_ml + r);
+            float2 ml[C::CLMAX];
+            float4 x[C::CLMAX];
+#pragma unroll
+            for (int s = 0; s < C::CLMAX; ++s) {               // every load in flight at once
+                ml[s] = make_float2(-INFINITY, 0.f);
+                x[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+                if (s < nsp) {
+                    ml[s] = ld_cluster_f2(cluster_map(ml_loc, (uint32_t)s));
+                    x[s] = ld_cluster_f4(cluster_map(o_loc, (uint32_t)s));
+                }
+            }
+            float M = -INFINITY;
+#pragma unroll
+            for (int s = 0; s < C::CLMAX; ++s)
+                if (ml[s].y > 0.f) M = fmaxf(M, ml[s].x);
+            float L = 0.f;
+            float4 O = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+            for (int s = 0; s < C::CLMAX; ++s) {
+                if (ml[s].y > 0.f) {
+                    const float f = ex2(ml[s].x - M);
+                    L = fmaf(f, ml[s].y, L);
+                    O.x = fmaf(f, x[s].x, O.x); O.y = fmaf(f, x[s].y, O.y);
+                    O.z = fmaf(f, x[s].z, O.z); O.w = fmaf(f, x[s].w, O.w);
+                }
+            }
+            const float inv = L == 0.f ? 0.f : 1.f / L;
+            reinterpret_cast<float4 *>(a.dst + (long long)b * a.dst_nb1 + (long long)(g * a.G + r) * D)[c] =
+                make_float4(O.x * inv, O.y * inv, O.z * inv, O.w * inv);
+        }
+        cluster_arrive();
+        cluster_wait();                                        // no CTA leaves while its partial is read
+        return;
+    }
 
     // ---- split arrival; the last CTA of this (stream, KV head) merges ----------
     int *s_last = reinterpret_cast<int *>(smem + C::MISC_OFF);

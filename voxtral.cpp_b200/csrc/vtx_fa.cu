@@ -402,6 +402,27 @@ int launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cud
     return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
 }
 
+// The same with the grid in clusters of `cs` CTAs along x.
+template <typename... KArgs, typename... Args>
+int launch_pdl_cluster(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, int cs,
+                       Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = (unsigned)cs;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 2;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...) == cudaSuccess ? VTX_OK : VTX_ERR_CUDA;
+}
+
 int encode_kv_map(CUtensorMap *m, const void *ptr, int D, int n_kv, int H, int Bk, size_t nb1, size_t nb2,
                   size_t nb3) {
     if (!g_encode) return VTX_ERR_CUDA;
@@ -814,10 +835,61 @@ int decode_batched_impl(const vtx_decode_batch *b, void *scratch, size_t scratch
 // wave covers the GPU, at least one 16-key tile per warp; workspace = the
 // split partials (O, then (m, l)) and one arrival counter per (stream, KV
 // head), which must be zero before the first call (every call leaves it so).
+// With the cluster merge (`cluster` > 1) the splits of a (stream, KV head) are
+// the CTAs of one cluster and the workspace is not used; its size is that of
+// the global merge either way, so the workspace query needs no device.
 struct LayerPlan {
     int n_splits = 1;
+    int cluster = 0;                            // > 1: splits per cluster (= the launch's n_splits)
     size_t o_bytes = 0, ml_bytes = 0, flag_bytes = 0, bytes = 0;
 };
+
+// Clusters of cs CTAs (cs = 1..8) of the decode-layer kernel of one cache
+// type that can be resident at once on the current device (one CTA per SM:
+// its shared memory), queried once per device.
+struct LayerClusters {
+    int max_active[LayerCfg<1>::CLMAX + 1];
+};
+
+template <int KVT>
+const LayerClusters *layer_clusters() {
+    using C = LayerCfg<KVT>;
+    static std::atomic<int> ready[kMaxDevices];              // 0 not yet, 1 done, 2 unavailable
+    static LayerClusters tab[kMaxDevices];
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    int st = ready[dev].load(std::memory_order_acquire);
+    if (st == 0) {
+        std::lock_guard<std::mutex> lk(mu);
+        st = ready[dev].load(std::memory_order_relaxed);
+        if (st == 0) {
+            bool ok = cudaFuncSetAttribute(fa_decode_layer_kernel<KVT, true>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) == cudaSuccess;
+            LayerClusters t{};
+            for (int cs = 1; ok && cs <= C::CLMAX; ++cs) {
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3((unsigned)cs);
+                cfg.blockDim = dim3(C::NT);
+                cfg.dynamicSmemBytes = C::SMEM;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = (unsigned)cs;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                ok = cudaOccupancyMaxActiveClusters(&t.max_active[cs], fa_decode_layer_kernel<KVT, true>, &cfg) ==
+                     cudaSuccess;
+            }
+            if (ok) tab[dev] = t;
+            else cudaGetLastError();
+            st = ok ? 1 : 2;
+            ready[dev].store(st, std::memory_order_release);
+        }
+    }
+    return st == 1 ? &tab[dev] : nullptr;
+}
 
 int check_layer_args(const vtx_decode_layer_args *p) {
     if (!p) return VTX_ERR_NULL;
@@ -831,7 +903,17 @@ int check_layer_args(const vtx_decode_layer_args *p) {
     return VTX_OK;
 }
 
-LayerPlan plan_layer(const vtx_decode_layer_args *p, int sms) {
+// Splits per (stream, KV head): enough for one wave over the SMs, at most one
+// per W tiles of max_kv_len.  With a cluster table: when that is at most
+// twice the largest cluster size cs whose clusters (one per (stream, KV head))
+// fit twice over -- this launch's and the next layer's, which then becomes
+// resident and streams its ring early -- the splits are min(splits, cs) CTAs
+// of one cluster, merged through distributed shared memory; otherwise the
+// global merge.  Measured on B200 (batch 1, 8 KV heads, graph replay, us per
+// layer, global / cluster of 6): F16 391 keys 5.70 / 4.28, 600 keys 6.01 /
+// 4.48; Q8_0 800 keys 7.78 / 6.35, 2000 keys 8.30 / 7.65; at 7300 Q8_0 keys
+// (18 splits) 11.56 / 16.32.
+LayerPlan plan_layer(const vtx_decode_layer_args *p, int sms, const LayerClusters *cl = nullptr) {
     LayerPlan lp;
     const long long items = (long long)p->n_seq * p->n_head_kv;
     const int tiles = (std::max(1, p->max_kv_len) + 15) / 16;
@@ -845,24 +927,33 @@ LayerPlan plan_layer(const vtx_decode_layer_args *p, int sms) {
         lp.o_bytes = align_up(rows * p->head_dim * 4, 256);
         lp.ml_bytes = align_up(rows * 8, 256);
         lp.flag_bytes = align_up((size_t)items * 4, 256);
+        if (cl) {
+            int fit = 0;
+            for (int cs = 2; cs <= LayerCfg<1>::CLMAX; ++cs)
+                if (cl->max_active[cs] >= 2 * items) fit = cs;
+            if (fit >= 2 && lp.n_splits <= 2 * fit) lp.cluster = std::min(lp.n_splits, fit);
+        }
     }
     lp.bytes = lp.o_bytes + lp.ml_bytes + lp.flag_bytes;
     return lp;
 }
 
 template <int KVT>
-int launch_decode_layer_t(const DecodeLayerArgs &a, unsigned ctas, cudaStream_t st) {
+int launch_decode_layer_t(const DecodeLayerArgs &a, unsigned ctas, int cluster, cudaStream_t st) {
     using C = LayerCfg<KVT>;
+    if (cluster > 1)                            // attribute set by layer_clusters()
+        return launch_pdl_cluster(fa_decode_layer_kernel<KVT, true>, dim3(ctas), dim3(C::NT), C::SMEM, st, cluster,
+                                  a);
     static std::atomic<int> attr_done[kMaxDevices];
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_done[dev].load(std::memory_order_acquire)) {
-        if (cudaFuncSetAttribute(fa_decode_layer_kernel<KVT>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
-            cudaSuccess)
+        if (cudaFuncSetAttribute(fa_decode_layer_kernel<KVT, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 C::SMEM) != cudaSuccess)
             return VTX_ERR_CUDA;
         attr_done[dev].store(1, std::memory_order_release);
     }
-    return launch_pdl(fa_decode_layer_kernel<KVT>, dim3(ctas), dim3(C::NT), C::SMEM, st, a);
+    return launch_pdl(fa_decode_layer_kernel<KVT, false>, dim3(ctas), dim3(C::NT), C::SMEM, st, a);
 }
 
 }  // namespace
@@ -1151,7 +1242,8 @@ int vtx_decode_layer(const vtx_decode_layer_args *p, void *workspace, size_t wor
     DeviceState *ds = nullptr;
     rc = ensure_device(&ds);
     if (rc != VTX_OK) return rc;
-    const LayerPlan lp = plan_layer(p, ds->sms);
+    const LayerClusters *cl = p->kv_type == VTX_TYPE_F16 ? layer_clusters<1>() : layer_clusters<8>();
+    const LayerPlan lp = plan_layer(p, ds->sms, cl);
     if (workspace_bytes < lp.bytes) return VTX_ERR_WORKSPACE;
     if (lp.bytes && (!workspace || reinterpret_cast<uintptr_t>(workspace) % 256)) return VTX_ERR_WORKSPACE;
     DecodeLayerArgs a{};
@@ -1164,18 +1256,19 @@ int vtx_decode_layer(const vtx_decode_layer_args *p, void *workspace, size_t wor
     a.theta_scale = std::pow(p->freq_base, -2.0f / (float)p->head_dim);   // as ggml: powf on the host
     a.cx = p->scale * kLog2e;
     a.dst = p->dst; a.dst_nb1 = (long long)(p->dst_nb1 / 4);
-    a.n_splits = lp.n_splits;
+    a.n_splits = lp.cluster > 1 ? lp.cluster : lp.n_splits;
     char *ws = static_cast<char *>(workspace);
-    if (lp.bytes) {
+    if (lp.bytes && lp.cluster <= 1) {
         a.part_o = reinterpret_cast<float *>(ws);
         a.part_ml = reinterpret_cast<float *>(ws + lp.o_bytes);
         a.flags = reinterpret_cast<unsigned *>(ws + lp.o_bytes + lp.ml_bytes);
     }
     a.early = p->early ? 1 : 0;
     a.err = ds->err;
-    const unsigned ctas = (unsigned)((long long)p->n_seq * p->n_head_kv * lp.n_splits);
+    const unsigned ctas = (unsigned)((long long)p->n_seq * p->n_head_kv * a.n_splits);
     cudaStream_t st = static_cast<cudaStream_t>(stream);
-    return p->kv_type == VTX_TYPE_F16 ? launch_decode_layer_t<1>(a, ctas, st) : launch_decode_layer_t<8>(a, ctas, st);
+    return p->kv_type == VTX_TYPE_F16 ? launch_decode_layer_t<1>(a, ctas, lp.cluster, st)
+                                      : launch_decode_layer_t<8>(a, ctas, lp.cluster, st);
 }
 
 int vtx_encoder_chunk_plan(int32_t total_mel_frames, vtx_enc_chunk *chunks, int32_t max_chunks,

@@ -13,7 +13,13 @@ the attention path for all layers once, as a CUDA graph:
     then:            vtx_decode_advance     (positions, ring slots, lengths + 1)
 
 and replays it per token with no host work: positions, ring slots and key
-counts live on the device and advance inside the graph.  Each of the n_seq
+counts live on the device and advance inside the graph.  The fused layer
+call's split layout follows a bound on the key counts (max_kv_len): the
+helper keeps one set of layer plans and one graph per bound, a power of two
+from 256 up to the window, and switches to the next as the caches grow (the
+host knows every stream's length from its start and the step count), so
+short caches run few splits merged inside a thread-block cluster and long
+ones many splits merged through global memory.  Each of the n_seq
 streams has its own cache per layer (rows = the window); the step's Q/K/V
 projections are read from fixed per-layer buffers that the caller (the rest
 of the decoder, out of scope here) fills before each replay.
@@ -45,6 +51,8 @@ class DecodeStepGraph:
         self.slots = (start % window).to(torch.int32).to(dev)
         self.kv_len = torch.clamp(start + 1, max=window).to(torch.int32).to(dev)   # includes the new token
         self._start = (self.positions.clone(), self.slots.clone(), self.kv_len.clone())
+        self._start_max = int(start.max()) if start.numel() else 0
+        self._steps = 0                         # steps since the start (or the last reset)
         # caches: [layer][stream] of window rows
         self.k_cache = torch.zeros((n_layers, n_seq, window, self.row), dtype=torch.uint8, device=dev)
         self.v_cache = torch.zeros_like(self.k_cache)
@@ -60,15 +68,7 @@ class DecodeStepGraph:
         self.out = torch.zeros_like(self.q)
         self.fused = fused and kv_type in (vtx_attn.F16, vtx_attn.Q8_0) and head_dim == 128
         self.plans: List[vtx_attn.DecodeBatchPlan] = []
-        self.layer_plans: List[vtx_attn.DecodeLayerPlan] = []
-        for l in range(n_layers if self.fused else 0):
-            # layer 0 follows vtx_decode_advance, which moves the counters: it
-            # waits before reading anything; later layers may stream their ring
-            # while the previous layer's kernel still runs
-            self.layer_plans.append(vtx_attn.DecodeLayerPlan(
-                [self.k_cache[l, s] for s in range(n_seq)], [self.v_cache[l, s] for s in range(n_seq)],
-                self.positions, self.slots, self.kv_len, n_head_q, n_head_kv, head_dim, kv_type, self.row, window,
-                head_dim ** -0.5, rope_base, early=l > 0))
+        self._layer_plans: dict = {}            # key bound -> one DecodeLayerPlan per layer
         for l in range(0 if self.fused else n_layers):
             p = vtx_attn.DecodeBatchPlan([self.k_cache[l, s] for s in range(n_seq)],
                                          [self.v_cache[l, s] for s in range(n_seq)], self.kv_len, n_head_q,
@@ -76,7 +76,7 @@ class DecodeStepGraph:
                                          fresh_row=self.slots)      # the append just before writes this row
             self.plans.append(p)
         self.stream = torch.cuda.Stream(device=dev)
-        self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self._graphs: dict = {}                 # key bound -> captured step
 
     def fill(self, layer: int, seq: int, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor) -> None:
         """Writes prefill tokens of one stream into one layer's ring (rows
@@ -88,8 +88,34 @@ class DecodeStepGraph:
         vtx_attn.kv_append(k, v, pos, pos % self.W, self.k_cache[layer, seq], self.v_cache[layer, seq],
                            self.kv_type, self.base, cache_nb1=self.row)
 
-    def _step_calls(self) -> None:
-        for l, lp in enumerate(self.layer_plans):
+    def bound(self) -> int:
+        """The key bound of the next step: the longest stream's kv_len after
+        it, rounded up to a power of two of at least 256, at most the window
+        (the two-call path uses the window)."""
+        if not self.fused:
+            return self.W
+        n = min(self._start_max + 1 + self._steps, self.W)
+        b = 256
+        while b < n:
+            b *= 2
+        return min(b, self.W)
+
+    def layer_plans(self, bound: int) -> List[vtx_attn.DecodeLayerPlan]:
+        """The fused layer calls planned for caches of at most `bound` rows."""
+        plans = self._layer_plans.get(bound)
+        if plans is None:
+            # layer 0 follows vtx_decode_advance, which moves the counters: it
+            # waits before reading anything; later layers may stream their ring
+            # while the previous layer's kernel still runs
+            plans = [vtx_attn.DecodeLayerPlan(
+                [self.k_cache[l, s] for s in range(self.S)], [self.v_cache[l, s] for s in range(self.S)],
+                self.positions, self.slots, self.kv_len, self.Hq, self.Hkv, self.D, self.kv_type, self.row, bound,
+                self.D ** -0.5, self.base, early=l > 0) for l in range(self.L)]
+            self._layer_plans[bound] = plans
+        return plans
+
+    def _step_calls(self, bound: int) -> None:
+        for l, lp in enumerate(self.layer_plans(bound) if self.fused else []):
             lp(self.q[l], self.k[l], self.v[l], self.out[l], self.stream)
         for l in range(0 if self.fused else self.L):
             vtx_attn.kv_append(self.k[l], self.v[l], self.positions, self.slots, None, None, self.kv_type, self.base,
@@ -110,34 +136,42 @@ class DecodeStepGraph:
             for dst, src in zip((self.positions, self.slots, self.kv_len), self._start):
                 dst.copy_(src)
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        self._steps = 0
 
     def step_eager(self) -> None:
         """One step issued call by call from the host (the uncaptured path)."""
+        bound = self.bound()
         self.stream.wait_stream(torch.cuda.current_stream(self.dev))
-        self._step_calls()
+        self._step_calls(bound)
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        self._steps += 1
 
-    def capture(self) -> None:
+    def capture(self, bound: int) -> None:
+        """Records one step with the plans of `bound` (nothing runs)."""
         torch.cuda.synchronize(self.dev)
-        self.graph = torch.cuda.CUDAGraph()
+        graph = torch.cuda.CUDAGraph()
         # the device counters must not move during capture: record only
-        with torch.cuda.graph(self.graph, stream=self.stream):
-            self._step_calls()
+        with torch.cuda.graph(graph, stream=self.stream):
+            self._step_calls(bound)
         torch.cuda.synchronize(self.dev)
+        self._graphs[bound] = graph
 
     def step(self) -> None:
-        """One decode step for every stream and layer.  The first step runs
-        eagerly (it also performs the library's one-time per-device set-up,
-        which a capture must not contain) and is then captured; every later
-        step is a graph replay."""
-        if self.graph is None:
+        """One decode step for every stream and layer.  The first step of each
+        key bound runs eagerly (it also performs the library's one-time
+        per-device set-up, which a capture must not contain) and is then
+        captured; every later step of that bound is a graph replay."""
+        bound = self.bound()
+        graph = self._graphs.get(bound)
+        if graph is None:
             self.step_eager()
-            self.capture()
+            self.capture(bound)
             return
         self.stream.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(self.stream):
-            self.graph.replay()
+            graph.replay()
         torch.cuda.current_stream(self.dev).wait_stream(self.stream)
+        self._steps += 1
 
 
 def _main() -> None:
