@@ -33,6 +33,17 @@ import torch
 import vtx_attn
 
 
+def key_bound(longest: int, window: int) -> int:
+    """The key bound a decode step's layer plans are made for: the longest
+    stream's kv_len rounded up to a power of two of at least 256, at most
+    the window."""
+    n = min(longest, window)
+    b = 256
+    while b < n:
+        b *= 2
+    return min(b, window)
+
+
 class DecodeStepGraph:
     def __init__(self, n_layers: int, n_seq: int, n_head_q: int, n_head_kv: int, head_dim: int, kv_type: int,
                  window: int, start_len, rope_base: float = 1e6, device: Optional[torch.device] = None,
@@ -94,11 +105,7 @@ class DecodeStepGraph:
         (the two-call path uses the window)."""
         if not self.fused:
             return self.W
-        n = min(self._start_max + 1 + self._steps, self.W)
-        b = 256
-        while b < n:
-            b *= 2
-        return min(b, self.W)
+        return key_bound(self._start_max + 1 + self._steps, self.W)
 
     def layer_plans(self, bound: int) -> List[vtx_attn.DecodeLayerPlan]:
         """The fused layer calls planned for caches of at most `bound` rows."""
